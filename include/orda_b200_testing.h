@@ -1,0 +1,26 @@
+/*
+ * orda_b200_testing.h - testing hook of the B200 distillation library (no counterpart in the
+ * reference). It exposes the library's tcgen05 GEMM on its own so the GPU tests can check each
+ * operand layout against a plain matrix product before the fused paths are checked.
+ */
+#ifndef ORDA_B200_TESTING_H_
+#define ORDA_B200_TESTING_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* out[m*ldo + n] = sum_k A(m, k) * B(n, k) in fp32, with 16-bit A/B (ORDA_BF16 / ORDA_F16).
+ * A(m, k) = A[m*lda + k] (a_mn == 0, K-major) or A[k*lda + m] (a_mn == 1, MN-major); B likewise.
+ * Enqueued on `stream`; pipeline timeouts are reported in *status. */
+int32_t orda_debug_gemm(int32_t dtype, int32_t a_mn, int32_t b_mn, const void* A, int64_t lda, const void* B,
+                        int64_t ldb, int64_t M, int64_t N, int64_t K, float* out, int64_t ldo, int32_t* status,
+                        void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ORDA_B200_TESTING_H_ */

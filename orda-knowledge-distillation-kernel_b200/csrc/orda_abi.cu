@@ -1,0 +1,637 @@
+// Host side of the C ABI (include/orda_b200.h): argument checks, workspace layout, TMA descriptor
+// encoding and the per-chunk launch sequence
+//
+//   logits GEMM + statistics epilogue -> row merge -> row losses -> [JSD sweep] -> dlogits sweep
+//   -> dH GEMM(s) -> dW GEMM(s)            ...per chunk, then one final reduction.
+//
+// It replaces the Python chunk loop of the reference autograd Functions
+// (ops/tied_teacher.py:366-516, ops/separate_teacher.py:589-700 and 849-968,
+// ops/precomputed_teacher.py:358-478).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+#include <type_traits>
+
+#include "gemm_tc.cuh"
+#include "orda_b200.h"
+#include "orda_b200_testing.h"
+#include "row_kernels.cuh"
+#include "simt_f32.cuh"
+
+using namespace orda;
+
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D tensor map over a row-major [outer, inner] array of 16-bit elements with a 128B-swizzled box.
+int make_map(CUtensorMap* m, int dtype, const void* base, uint64_t inner, uint64_t outer, uint64_t ld_elems,
+             uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return ORDA_ERR_CUDA;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (ld_elems * 2) % 16 != 0) return ORDA_ERR_ALIGNMENT;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {ld_elems * 2};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(m, dtype == ORDA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                        const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? ORDA_OK : ORDA_ERR_INVALID_ARGUMENT;
+}
+
+// Operand map: K-major [mn, k] (k contiguous) or MN-major [k, mn] (mn contiguous).
+int make_operand_map(CUtensorMap* m, int dtype, const void* base, bool mn_major, int64_t mn, int64_t k, int64_t ld,
+                     int tile_mn) {
+  if (mn_major) return make_map(m, dtype, base, mn, k, ld, 64, 64);
+  return make_map(m, dtype, base, k, mn, ld, 64, tile_mn);
+}
+
+int num_sms() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+size_t esize(int dtype) { return dtype == ORDA_F32 ? 4 : 2; }
+
+constexpr int64_t kDefaultWorkspaceLogitBytes = int64_t(2) << 30;  // bound of the logits chunk buffers
+
+struct Plan {
+  // problem classification
+  bool teacher;        // teacher logits exist
+  bool teacher_gmem;   // from caller memory
+  bool teacher_acc;    // from a second accumulator
+  bool teacher_ce;
+  bool kl, jsd, rev, t_not_one;
+  bool grad_s, grad_t, any_grad;
+  bool write_ws_s, write_ws_t;
+  uint32_t flags;
+  // layout
+  int64_t C, n_vtiles, vpad;
+  size_t off_row_losses, off_tile_stats, off_label, off_row_stats, off_row_sums, off_ws_s, off_ws_t, total;
+};
+
+int check_args(const orda_distill_args_t* a) {
+  if (!a || a->abi_version != ORDA_ABI_VERSION) return ORDA_ERR_INVALID_ARGUMENT;
+  if (a->n_rows <= 0 || a->hidden <= 0 || a->vocab <= 0) return ORDA_ERR_INVALID_ARGUMENT;
+  if (a->compute_dtype != ORDA_F32 && a->compute_dtype != ORDA_F16 && a->compute_dtype != ORDA_BF16)
+    return ORDA_ERR_INVALID_ARGUMENT;
+  if (!a->student_hidden || !a->weight || !a->labels || !a->out_reduced || !a->device_status)
+    return ORDA_ERR_INVALID_ARGUMENT;
+  if (a->teacher_mode < ORDA_TEACHER_TIED || a->teacher_mode > ORDA_TEACHER_HIDDEN) return ORDA_ERR_INVALID_ARGUMENT;
+  if (a->vocab_offset < 0 || a->vocab_total < a->vocab_offset + a->vocab) return ORDA_ERR_INVALID_ARGUMENT;
+  if (!(a->kl_temperature > 0.f) || a->student_ce_weight < 0.f || a->teacher_ce_weight < 0.f || a->kl_weight < 0.f)
+    return ORDA_ERR_INVALID_ARGUMENT;
+  if (a->divergence < ORDA_DIV_FORWARD || a->divergence > ORDA_DIV_JSD) return ORDA_ERR_INVALID_ARGUMENT;
+  if (a->divergence == ORDA_DIV_JSD && !(a->jsd_beta >= 0.f && a->jsd_beta <= 1.f)) return ORDA_ERR_INVALID_ARGUMENT;
+  if (a->teacher_mode == ORDA_TEACHER_LOGITS && a->teacher_ce_weight != 0.f) return ORDA_ERR_UNSUPPORTED;
+  if (a->teacher_mode == ORDA_TEACHER_HIDDEN && a->teacher_ce_weight != 0.f) return ORDA_ERR_UNSUPPORTED;
+  return ORDA_OK;
+}
+
+Plan make_plan(const orda_distill_args_t* a, int64_t chunk_override) {
+  Plan p{};
+  const int mode = a->teacher_mode;
+  p.teacher_ce = a->teacher_ce_weight != 0.f;
+  p.kl = a->kl_weight != 0.f;
+  p.teacher = p.kl || p.teacher_ce;
+  p.teacher_gmem = p.teacher && mode == ORDA_TEACHER_LOGITS;
+  p.teacher_acc = p.teacher && !p.teacher_gmem;
+  p.t_not_one = a->kl_temperature != 1.f;
+  const bool beta_edge0 = a->divergence == ORDA_DIV_JSD && a->jsd_beta == 0.f;
+  const bool beta_edge1 = a->divergence == ORDA_DIV_JSD && a->jsd_beta == 1.f;
+  p.jsd = p.kl && a->divergence == ORDA_DIV_JSD && !beta_edge0 && !beta_edge1;
+  p.rev = p.kl && (a->divergence == ORDA_DIV_REVERSE || beta_edge1);
+  p.grad_s = a->need_grad_student_hidden || a->need_grad_weight;
+  const bool tied = mode == ORDA_TEACHER_TIED, sep = mode == ORDA_TEACHER_SEPARATE;
+  p.grad_t = p.teacher_ce && ((tied && (a->need_grad_teacher_hidden || a->need_grad_weight)) ||
+                              (sep && (a->need_grad_teacher_hidden || a->need_grad_teacher_weight)));
+  p.any_grad = p.grad_s || p.grad_t;
+  p.write_ws_s = p.grad_s || p.jsd || p.grad_t;  // grad sweep / JSD sweep read the student row
+  p.write_ws_t = p.teacher_acc && (p.grad_t || (p.kl && (p.grad_s || p.jsd)));
+  uint32_t f = 0;
+  if (p.teacher) f |= F_TEACHER;
+  if (p.teacher_gmem) f |= F_TEACHER_GMEM;
+  if (p.teacher_ce) f |= F_TEACHER_CE;
+  if (p.kl) f |= F_KL;
+  if (p.t_not_one) f |= F_T_NOT_ONE;
+  if (p.rev) f |= F_KL_REVERSE;
+  if (p.jsd) f |= F_JSD;
+  if (p.write_ws_s) f |= F_WRITE_WS_S;
+  if (p.write_ws_t) f |= F_WRITE_WS_T;
+  if (p.grad_s) f |= F_GRAD_S;
+  if (p.grad_t) f |= F_GRAD_T;
+  if (a->validate_labels) f |= F_VALIDATE;
+  p.flags = f;
+
+  p.n_vtiles = cdiv(a->vocab, kVocabTile);
+  p.vpad = p.n_vtiles * kVocabTile;
+  const size_t es = esize(a->compute_dtype);
+  const int64_t bufs = (p.write_ws_s || a->compute_dtype == ORDA_F32 ? 1 : 0) + (p.teacher_acc ? 1 : 0);
+  int64_t C = chunk_override > 0 ? chunk_override : a->chunk_rows;
+  if (C <= 0) {
+    const int64_t per_row = std::max<int64_t>(1, bufs) * p.vpad * (int64_t)es;
+    C = std::max<int64_t>(kTileRows, (kDefaultWorkspaceLogitBytes / per_row) / kTileRows * kTileRows);
+  }
+  p.C = std::min<int64_t>(C, a->n_rows);
+
+  size_t off = 0;
+  p.off_row_losses = off; off = align256(off + sizeof(float) * 3 * a->n_rows);
+  p.off_tile_stats = off; off = align256(off + sizeof(float) * p.C * p.n_vtiles * kTileStats);
+  p.off_label = off; off = align256(off + sizeof(float) * 2 * p.C);
+  p.off_row_stats = off; off = align256(off + sizeof(float) * kRowStats * p.C);
+  p.off_row_sums = off; off = align256(off + sizeof(float) * 2 * p.C);
+  // the fp32 path materialises raw logits, so it always needs the student (and teacher) buffer
+  const bool need_s = p.write_ws_s || a->compute_dtype == ORDA_F32;
+  const bool need_t = p.teacher_acc && (p.write_ws_t || a->compute_dtype == ORDA_F32);
+  p.off_ws_s = off; if (need_s) off = align256(off + es * p.C * p.vpad);
+  p.off_ws_t = off; if (need_t) off = align256(off + es * p.C * p.vpad);
+  p.total = off;
+  return p;
+}
+
+template <typename Kernel>
+void set_smem(Kernel k, uint32_t bytes) {
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+}
+
+template <int BN, bool A_MN, bool B_MN, int MODE, int EPI, typename T16>
+int launch_tc(TcGemmParams& prm, int64_t M, int64_t N, cudaStream_t stream, int group_m) {
+  using S = GemmShape<BN, MODE>;
+  prm.m_tiles = static_cast<int32_t>(cdiv(M, kTileRows));
+  prm.n_tiles = static_cast<int32_t>(cdiv(N, BN));
+  prm.group_m = group_m;
+  const int64_t tiles = (int64_t)prm.m_tiles * prm.n_tiles;
+  if (tiles <= 0) return ORDA_OK;
+  if (tiles > INT32_MAX) return ORDA_ERR_UNSUPPORTED;
+  auto k = tc_gemm_kernel<BN, A_MN, B_MN, MODE, EPI, T16>;
+  set_smem(k, S::kSmemBytes);
+  const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms()));
+  k<<<grid, kGemmThreads, S::kSmemBytes, stream>>>(prm);
+  return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
+}
+
+struct ChunkPtrs {
+  const uint8_t* hs; const uint8_t* ht; const int64_t* labels;
+  int64_t r0, rows;
+  uint8_t* grad_hs; uint8_t* grad_ht;
+  const uint8_t* tg;
+};
+
+RowParams row_params(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const ChunkPtrs& c) {
+  RowParams r{};
+  r.rows = c.rows;
+  r.vocab = a->vocab; r.vocab_offset = a->vocab_offset; r.vocab_total = a->vocab_total;
+  r.ignore_index = a->ignore_index;
+  r.n_vtiles = static_cast<int32_t>(P.n_vtiles);
+  r.flags = P.flags;
+  r.temperature = a->kl_temperature; r.inv_t = 1.f / a->kl_temperature;
+  r.jsd_beta = a->jsd_beta;
+  r.w_s = a->student_ce_weight; r.w_t = a->teacher_ce_weight; r.w_kl = a->kl_weight;
+  r.labels = c.labels;
+  r.tile_stats = reinterpret_cast<float*>(ws + P.off_tile_stats);
+  r.label_logits = reinterpret_cast<float*>(ws + P.off_label);
+  r.row_stats = reinterpret_cast<float*>(ws + P.off_row_stats);
+  r.row_sums = reinterpret_cast<float*>(ws + P.off_row_sums);
+  float* rl = a->out_row_losses ? a->out_row_losses : reinterpret_cast<float*>(ws + P.off_row_losses);
+  r.row_losses = rl + c.r0;
+  r.ld_row_losses = a->n_rows;
+  r.ws_s = ws + P.off_ws_s; r.ws_t = ws + P.off_ws_t; r.ld_ws = P.vpad;
+  r.t_gmem = c.tg; r.ld_tg = a->ld_teacher_logits; r.tg_dtype = a->teacher_logits_dtype;
+  r.status = a->device_status;
+  return r;
+}
+
+FwdEpiParams fwd_params(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const ChunkPtrs& c) {
+  FwdEpiParams f{};
+  f.rows = c.rows;
+  f.vocab = a->vocab; f.vocab_offset = a->vocab_offset; f.vocab_total = a->vocab_total;
+  f.ignore_index = a->ignore_index;
+  f.n_vtiles = static_cast<int32_t>(P.n_vtiles);
+  f.flags = P.flags;
+  f.inv_t = 1.f / a->kl_temperature;
+  f.labels = c.labels;
+  f.ws_s = ws + P.off_ws_s; f.ws_t = ws + P.off_ws_t; f.ld_ws = P.vpad;
+  f.t_gmem = c.tg; f.ld_tg = a->ld_teacher_logits; f.tg_dtype = a->teacher_logits_dtype;
+  f.tile_stats = reinterpret_cast<float*>(ws + P.off_tile_stats);
+  f.label_logits = reinterpret_cast<float*>(ws + P.off_label);
+  return f;
+}
+
+// ------------------------------------------------------------------ 16-bit (tensor core) phases
+template <typename T16>
+int forward_tc(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const ChunkPtrs& c, cudaStream_t s) {
+  const int dt = a->compute_dtype;
+  TcGemmParams prm{};
+  prm.status = a->device_status;
+  prm.fwd = fwd_params(a, P, ws, c);
+  int rc;
+  if ((rc = make_operand_map(&prm.a0, dt, c.hs, false, c.rows, a->hidden, a->ld_student_hidden, kTileRows))) return rc;
+  if ((rc = make_operand_map(&prm.b0, dt, a->weight, false, a->vocab, a->hidden, a->ld_weight, kVocabTile))) return rc;
+  prm.kb0 = static_cast<int32_t>(cdiv(a->hidden, kBK));
+  if (P.teacher_acc && a->teacher_mode == ORDA_TEACHER_TIED) {
+    if ((rc = make_operand_map(&prm.a1, dt, c.ht, false, c.rows, a->hidden, a->ld_teacher_hidden, kTileRows))) return rc;
+    return launch_tc<kVocabTile, false, false, GM_SHARED_B, EPI_FWD_STATS, T16>(prm, c.rows, a->vocab, s, 16);
+  }
+  if (P.teacher_acc) {
+    if ((rc = make_operand_map(&prm.a1, dt, c.ht, false, c.rows, a->teacher_hidden, a->ld_teacher_hidden, kTileRows))) return rc;
+    if ((rc = make_operand_map(&prm.b1, dt, a->teacher_weight, false, a->vocab, a->teacher_hidden, a->ld_teacher_weight, kVocabTile))) return rc;
+    prm.kb1 = static_cast<int32_t>(cdiv(a->teacher_hidden, kBK));
+    return launch_tc<kVocabTile, false, false, GM_TWO_ACC, EPI_FWD_STATS, T16>(prm, c.rows, a->vocab, s, 16);
+  }
+  return launch_tc<kVocabTile, false, false, GM_SINGLE, EPI_FWD_STATS, T16>(prm, c.rows, a->vocab, s, 16);
+}
+
+// dH[rows, N] = dZ[rows, V] * Wm[V, N]
+template <typename T16>
+int dh_tc(const orda_distill_args_t* a, const Plan& P, const void* dz, const void* wmat, int64_t ldw, int64_t n,
+          void* out, int64_t rows, int32_t* status, cudaStream_t s) {
+  TcGemmParams prm{};
+  prm.status = status;
+  int rc;
+  if ((rc = make_operand_map(&prm.a0, a->compute_dtype, dz, false, rows, a->vocab, P.vpad, kTileRows))) return rc;
+  if ((rc = make_operand_map(&prm.b0, a->compute_dtype, wmat, true, n, a->vocab, ldw, 256))) return rc;
+  prm.kb0 = static_cast<int32_t>(cdiv(a->vocab, kBK));
+  prm.st = StoreEpiParams{out, n, rows, n, 0, 0};
+  return launch_tc<256, false, true, GM_SINGLE, EPI_STORE, T16>(prm, rows, n, s, 8);
+}
+
+// dW[V, N] (+)= dZ0^T H0 (+ dZ1^T H1)
+template <typename T16>
+int dw_tc(const orda_distill_args_t* a, const Plan& P, const void* dz0, const void* h0, int64_t ldh0, const void* dz1,
+          const void* h1, int64_t ldh1, int64_t n, void* out, int out_f32, int accumulate, int64_t rows,
+          int32_t* status, cudaStream_t s) {
+  TcGemmParams prm{};
+  prm.status = status;
+  const int dt = a->compute_dtype;
+  int rc;
+  if ((rc = make_operand_map(&prm.a0, dt, dz0, true, a->vocab, rows, P.vpad, kTileRows))) return rc;
+  if ((rc = make_operand_map(&prm.b0, dt, h0, true, n, rows, ldh0, 256))) return rc;
+  prm.kb0 = static_cast<int32_t>(cdiv(rows, kBK));
+  prm.st = StoreEpiParams{out, n, a->vocab, n, out_f32, accumulate};
+  if (dz1) {
+    if ((rc = make_operand_map(&prm.a1, dt, dz1, true, a->vocab, rows, P.vpad, kTileRows))) return rc;
+    if ((rc = make_operand_map(&prm.b1, dt, h1, true, n, rows, ldh1, 256))) return rc;
+    prm.kb1 = prm.kb0;
+    return launch_tc<256, true, true, GM_TWO_SEG, EPI_STORE, T16>(prm, a->vocab, n, s, 8);
+  }
+  return launch_tc<256, true, true, GM_SINGLE, EPI_STORE, T16>(prm, a->vocab, n, s, 8);
+}
+
+// ------------------------------------------------------------------ fp32 (SIMT) phases
+void simt_gemm(const float* A, int64_t sam, int64_t sak, const float* B, int64_t sbn, int64_t sbk, float* out,
+               int64_t ldo, int64_t M, int64_t N, int64_t K, int accumulate, cudaStream_t s) {
+  dim3 grid(static_cast<unsigned>(cdiv(N, kSimtTile)), static_cast<unsigned>(cdiv(M, kSimtTile)));
+  simt_gemm_f32_kernel<<<grid, 256, 0, s>>>(A, sam, sak, B, sbn, sbk, out, ldo, M, N, K, accumulate);
+}
+
+int forward_f32(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const ChunkPtrs& c, cudaStream_t s) {
+  float* ws_s = reinterpret_cast<float*>(ws + P.off_ws_s);
+  float* ws_t = reinterpret_cast<float*>(ws + P.off_ws_t);
+  simt_gemm(reinterpret_cast<const float*>(c.hs), a->ld_student_hidden, 1, static_cast<const float*>(a->weight),
+            a->ld_weight, 1, ws_s, P.vpad, c.rows, a->vocab, a->hidden, 0, s);
+  if (P.teacher_acc) {
+    const bool tied = a->teacher_mode == ORDA_TEACHER_TIED;
+    const float* wt = static_cast<const float*>(tied ? a->weight : a->teacher_weight);
+    const int64_t ldwt = tied ? a->ld_weight : a->ld_teacher_weight;
+    const int64_t kt = tied ? a->hidden : a->teacher_hidden;
+    simt_gemm(reinterpret_cast<const float*>(c.ht), a->ld_teacher_hidden, 1, wt, ldwt, 1, ws_t, P.vpad, c.rows,
+              a->vocab, kt, 0, s);
+  }
+  FwdEpiParams f = fwd_params(a, P, ws, c);
+  f.flags |= F_WRITE_WS_S | (P.teacher_acc ? F_WRITE_WS_T : 0u);  // shift in place
+  const int64_t total = c.rows * P.n_vtiles;
+  const int grid = static_cast<int>(std::min<int64_t>(cdiv(total, 128), 8192));
+  if (P.teacher_acc) fwd_stats_gmem_kernel<true><<<grid, 128, 0, s>>>(f);
+  else fwd_stats_gmem_kernel<false><<<grid, 128, 0, s>>>(f);
+  return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
+}
+
+// ------------------------------------------------------------------ shared row phases
+template <typename WsT>
+int row_phases(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const ChunkPtrs& c, cudaStream_t s,
+               bool do_merge, bool do_loss_and_sweeps, const float* row_stats_ext, const float* row_sums_ext) {
+  RowParams r = row_params(a, P, ws, c);
+  if (do_merge) {
+    const int grid = static_cast<int>(std::min<int64_t>(cdiv(c.rows, 8), 65535));
+    row_merge_kernel<<<grid, 256, 0, s>>>(r);
+  }
+  if (!do_loss_and_sweeps) return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
+  if (row_stats_ext) r.row_stats = const_cast<float*>(row_stats_ext);
+  const size_t sweep_smem = sizeof(float) * (2 * P.n_vtiles + 32);
+  const int sweep_grid = static_cast<int>(std::min<int64_t>(c.rows, 8 * num_sms()));
+  if (P.jsd && !row_sums_ext) {
+    float* sums = reinterpret_cast<float*>(ws + P.off_row_sums);
+    set_smem(jsd_sweep_kernel<WsT>, static_cast<uint32_t>(sweep_smem));
+    jsd_sweep_kernel<WsT><<<sweep_grid, 256, sweep_smem, s>>>(r, sums);
+  }
+  if (row_sums_ext) r.row_sums = row_sums_ext;
+  row_loss_kernel<<<static_cast<int>(cdiv(c.rows, 256)), 256, 0, s>>>(r);
+  if (P.any_grad) {
+    set_smem(grad_sweep_kernel<WsT>, static_cast<uint32_t>(sweep_smem));
+    grad_sweep_kernel<WsT><<<sweep_grid, 256, sweep_smem, s>>>(r);
+  }
+  return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
+}
+
+template <typename WsT>
+int grad_gemms(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const ChunkPtrs& c, bool first_chunk,
+               cudaStream_t s) {
+  const bool tied = a->teacher_mode == ORDA_TEACHER_TIED;
+  const bool sep = a->teacher_mode == ORDA_TEACHER_SEPARATE;
+  void* ws_s = ws + P.off_ws_s;
+  void* ws_t = ws + P.off_ws_t;
+  const int acc = first_chunk ? 0 : 1;
+  int rc = ORDA_OK;
+  if constexpr (std::is_same<WsT, float>::value) {
+    const float* zs = static_cast<const float*>(ws_s);
+    const float* zt = static_cast<const float*>(ws_t);
+    const float* W = static_cast<const float*>(a->weight);
+    const float* Wt = static_cast<const float*>(a->teacher_weight);
+    if (a->need_grad_student_hidden)
+      simt_gemm(zs, P.vpad, 1, W, 1, a->ld_weight, reinterpret_cast<float*>(c.grad_hs), a->hidden, c.rows, a->hidden,
+                a->vocab, 0, s);
+    if (a->need_grad_weight) {
+      simt_gemm(zs, 1, P.vpad, reinterpret_cast<const float*>(c.hs), 1, a->ld_student_hidden,
+                static_cast<float*>(a->grad_weight), a->hidden, a->vocab, a->hidden, c.rows, acc, s);
+      if (tied && P.grad_t)
+        simt_gemm(zt, 1, P.vpad, reinterpret_cast<const float*>(c.ht), 1, a->ld_teacher_hidden,
+                  static_cast<float*>(a->grad_weight), a->hidden, a->vocab, a->hidden, c.rows, 1, s);
+    }
+    if (P.grad_t && a->need_grad_teacher_hidden) {
+      const float* wm = tied ? W : Wt;
+      const int64_t ldm = tied ? a->ld_weight : a->ld_teacher_weight;
+      simt_gemm(zt, P.vpad, 1, wm, 1, ldm, reinterpret_cast<float*>(c.grad_ht), a->teacher_hidden, c.rows,
+                a->teacher_hidden, a->vocab, 0, s);
+    }
+    if (sep && P.grad_t && a->need_grad_teacher_weight)
+      simt_gemm(zt, 1, P.vpad, reinterpret_cast<const float*>(c.ht), 1, a->ld_teacher_hidden,
+                static_cast<float*>(a->grad_teacher_weight), a->teacher_hidden, a->vocab, a->teacher_hidden, c.rows,
+                acc, s);
+    rc = cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
+  } else {
+    int32_t* st = a->device_status;
+    if (a->need_grad_student_hidden)
+      if ((rc = dh_tc<WsT>(a, P, ws_s, a->weight, a->ld_weight, a->hidden, c.grad_hs, c.rows, st, s))) return rc;
+    if (a->need_grad_weight) {
+      const bool two = tied && P.grad_t;
+      if ((rc = dw_tc<WsT>(a, P, ws_s, c.hs, a->ld_student_hidden, two ? ws_t : nullptr, two ? c.ht : nullptr,
+                           a->ld_teacher_hidden, a->hidden, a->grad_weight, a->grad_weight_fp32, acc, c.rows, st, s)))
+        return rc;
+    }
+    if (P.grad_t && a->need_grad_teacher_hidden) {
+      const void* wm = tied ? a->weight : a->teacher_weight;
+      const int64_t ldm = tied ? a->ld_weight : a->ld_teacher_weight;
+      if ((rc = dh_tc<WsT>(a, P, ws_t, wm, ldm, a->teacher_hidden, c.grad_ht, c.rows, st, s))) return rc;
+    }
+    if (sep && P.grad_t && a->need_grad_teacher_weight)
+      if ((rc = dw_tc<WsT>(a, P, ws_t, c.ht, a->ld_teacher_hidden, nullptr, nullptr, 0, a->teacher_hidden,
+                           a->grad_teacher_weight, a->grad_weight_fp32, acc, c.rows, st, s)))
+        return rc;
+  }
+  // tied teacher with teacher CE off: the reference returns an all-zero teacher-hidden gradient
+  if (tied && a->need_grad_teacher_hidden && !P.grad_t)
+    cudaMemsetAsync(c.grad_ht, 0, esize(a->compute_dtype) * c.rows * a->teacher_hidden, s);
+  return rc;
+}
+
+ChunkPtrs chunk_ptrs(const orda_distill_args_t* a, int64_t r0, int64_t rows) {
+  const size_t es = esize(a->compute_dtype);
+  ChunkPtrs c{};
+  c.r0 = r0;
+  c.rows = rows;
+  c.hs = static_cast<const uint8_t*>(a->student_hidden) + es * r0 * a->ld_student_hidden;
+  c.ht = a->teacher_hidden_ptr ? static_cast<const uint8_t*>(a->teacher_hidden_ptr) + es * r0 * a->ld_teacher_hidden
+                               : nullptr;
+  c.labels = a->labels + r0;
+  c.grad_hs = a->grad_student_hidden ? static_cast<uint8_t*>(a->grad_student_hidden) + es * r0 * a->hidden : nullptr;
+  c.grad_ht = a->grad_teacher_hidden ? static_cast<uint8_t*>(a->grad_teacher_hidden) + es * r0 * a->teacher_hidden
+                                     : nullptr;
+  c.tg = a->teacher_logits
+             ? static_cast<const uint8_t*>(a->teacher_logits) + esize(a->teacher_logits_dtype) * r0 * a->ld_teacher_logits
+             : nullptr;
+  return c;
+}
+
+int check_operands(const orda_distill_args_t* a, const Plan& P) {
+  const bool needs_t_hidden = P.teacher_acc || (a->teacher_mode == ORDA_TEACHER_TIED && a->need_grad_teacher_hidden);
+  if (needs_t_hidden && !a->teacher_hidden_ptr) return ORDA_ERR_INVALID_ARGUMENT;
+  if (P.teacher_acc && a->teacher_mode != ORDA_TEACHER_TIED && !a->teacher_weight) return ORDA_ERR_INVALID_ARGUMENT;
+  if (P.teacher_gmem && !a->teacher_logits) return ORDA_ERR_INVALID_ARGUMENT;
+  if (a->need_grad_student_hidden && !a->grad_student_hidden) return ORDA_ERR_INVALID_ARGUMENT;
+  if (a->need_grad_weight && !a->grad_weight) return ORDA_ERR_INVALID_ARGUMENT;
+  if (a->need_grad_teacher_hidden && !a->grad_teacher_hidden) return ORDA_ERR_INVALID_ARGUMENT;
+  if (a->need_grad_teacher_weight && !a->grad_teacher_weight) return ORDA_ERR_INVALID_ARGUMENT;
+  if (a->compute_dtype != ORDA_F32) {
+    if (a->hidden % 8 || a->ld_student_hidden % 8 || a->ld_weight % 8) return ORDA_ERR_ALIGNMENT;
+    if (P.teacher_acc && (a->teacher_hidden % 8 || a->ld_teacher_hidden % 8)) return ORDA_ERR_ALIGNMENT;
+    if (P.teacher_acc && a->teacher_mode != ORDA_TEACHER_TIED && a->ld_teacher_weight % 8) return ORDA_ERR_ALIGNMENT;
+    if (a->grad_weight_fp32 == 0 && a->need_grad_weight == 0) { /* nothing */ }
+  } else if (a->grad_weight_fp32 == 0 && (a->need_grad_weight || a->need_grad_teacher_weight)) {
+    return ORDA_ERR_INVALID_ARGUMENT;  // fp32 path accumulates weight gradients in fp32
+  }
+  return ORDA_OK;
+}
+
+template <typename WsT>
+int run_all(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, cudaStream_t s) {
+  int rc;
+  for (int64_t r0 = 0; r0 < a->n_rows; r0 += P.C) {
+    const int64_t rows = std::min<int64_t>(P.C, a->n_rows - r0);
+    const ChunkPtrs c = chunk_ptrs(a, r0, rows);
+    if constexpr (std::is_same<WsT, float>::value) rc = forward_f32(a, P, ws, c, s);
+    else rc = forward_tc<WsT>(a, P, ws, c, s);
+    if (rc) return rc;
+    if ((rc = row_phases<WsT>(a, P, ws, c, s, true, true, nullptr, nullptr))) return rc;
+    if ((rc = grad_gemms<WsT>(a, P, ws, c, r0 == 0, s))) return rc;
+  }
+  const float* rl = a->out_row_losses ? a->out_row_losses : reinterpret_cast<const float*>(ws + P.off_row_losses);
+  finalize_kernel<<<1, 1024, 0, s>>>(rl, a->n_rows, a->labels, a->n_rows, a->ignore_index, a->reduction, P.flags,
+                                     a->student_ce_weight, a->teacher_ce_weight, a->kl_weight, a->out_reduced);
+  return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
+}
+
+int dispatch_all(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, cudaStream_t s) {
+  switch (a->compute_dtype) {
+    case ORDA_BF16: return run_all<__nv_bfloat16>(a, P, ws, s);
+    case ORDA_F16: return run_all<__half>(a, P, ws, s);
+    default: return run_all<float>(a, P, ws, s);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t orda_abi_version(void) { return ORDA_ABI_VERSION; }
+
+size_t orda_args_struct_size(void) { return sizeof(orda_distill_args_t); }
+
+const char* orda_status_string(int32_t status) {
+  switch (status) {
+    case ORDA_OK: return "ok";
+    case ORDA_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case ORDA_ERR_ALIGNMENT: return "16-bit operands need 16-byte aligned bases and row strides that are multiples of 8 elements";
+    case ORDA_ERR_WORKSPACE: return "workspace too small";
+    case ORDA_ERR_UNSUPPORTED: return "unsupported configuration";
+    case ORDA_ERR_CUDA: return "CUDA launch error";
+    case ORDA_ERR_TIMEOUT: return "device pipeline wait timed out";
+    case ORDA_ERR_LABEL_RANGE: return "label outside [0, vocab) that is not ignore_index";
+    case ORDA_ERR_NO_DEVICE: return "no CUDA device";
+    default: return "unknown status";
+  }
+}
+
+size_t orda_distill_workspace_bytes(const orda_distill_args_t* args) {
+  if (check_args(args) != ORDA_OK) return 0;
+  return make_plan(args, 0).total;
+}
+
+int32_t orda_distill_fwdbwd(const orda_distill_args_t* args, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_args(args);
+  if (rc) return rc;
+  const Plan P = make_plan(args, 0);
+  if ((rc = check_operands(args, P))) return rc;
+  if (!workspace || workspace_bytes < P.total) return ORDA_ERR_WORKSPACE;
+  return dispatch_all(args, P, static_cast<uint8_t*>(workspace), static_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------------------- vocab-sharded phases
+size_t orda_shard_workspace_bytes(const orda_distill_args_t* args) {
+  if (check_args(args) != ORDA_OK) return 0;
+  return make_plan(args, args->n_rows).total;
+}
+
+int32_t orda_shard_forward(const orda_distill_args_t* args, void* workspace, size_t workspace_bytes,
+                           float* row_stats, void* stream) {
+  int rc = check_args(args);
+  if (rc) return rc;
+  const Plan P = make_plan(args, args->n_rows);
+  if ((rc = check_operands(args, P))) return rc;
+  if (!workspace || workspace_bytes < P.total || !row_stats) return ORDA_ERR_WORKSPACE;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const ChunkPtrs c = chunk_ptrs(args, 0, args->n_rows);
+  switch (args->compute_dtype) {
+    case ORDA_BF16: rc = forward_tc<__nv_bfloat16>(args, P, ws, c, s); if (!rc) rc = row_phases<__nv_bfloat16>(args, P, ws, c, s, true, false, nullptr, nullptr); break;
+    case ORDA_F16: rc = forward_tc<__half>(args, P, ws, c, s); if (!rc) rc = row_phases<__half>(args, P, ws, c, s, true, false, nullptr, nullptr); break;
+    default: rc = forward_f32(args, P, ws, c, s); if (!rc) rc = row_phases<float>(args, P, ws, c, s, true, false, nullptr, nullptr); break;
+  }
+  if (rc) return rc;
+  cudaMemcpyAsync(row_stats, ws + P.off_row_stats, sizeof(float) * kRowStats * args->n_rows, cudaMemcpyDeviceToDevice, s);
+  return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
+}
+
+int32_t orda_merge_row_stats(const float* gathered, int32_t world, int64_t n_rows, float* row_stats, void* stream) {
+  if (!gathered || !row_stats || world < 1 || n_rows <= 0) return ORDA_ERR_INVALID_ARGUMENT;
+  const int grid = static_cast<int>(std::min<int64_t>(cdiv(n_rows, 256), 65535));
+  merge_records_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(gathered, world, n_rows, row_stats);
+  return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
+}
+
+int32_t orda_shard_jsd_partials(const orda_distill_args_t* args, void* workspace, size_t workspace_bytes,
+                                const float* row_stats, float* row_sums, void* stream) {
+  int rc = check_args(args);
+  if (rc) return rc;
+  const Plan P = make_plan(args, args->n_rows);
+  if (!workspace || workspace_bytes < P.total || !row_stats || !row_sums) return ORDA_ERR_WORKSPACE;
+  if (!P.jsd) return ORDA_OK;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const ChunkPtrs c = chunk_ptrs(args, 0, args->n_rows);
+  RowParams r = row_params(args, P, ws, c);
+  r.row_stats = const_cast<float*>(row_stats);
+  const size_t smem = sizeof(float) * (2 * P.n_vtiles + 32);
+  const int grid = static_cast<int>(std::min<int64_t>(c.rows, 8 * num_sms()));
+  switch (args->compute_dtype) {
+    case ORDA_BF16: set_smem(jsd_sweep_kernel<__nv_bfloat16>, (uint32_t)smem); jsd_sweep_kernel<__nv_bfloat16><<<grid, 256, smem, s>>>(r, row_sums); break;
+    case ORDA_F16: set_smem(jsd_sweep_kernel<__half>, (uint32_t)smem); jsd_sweep_kernel<__half><<<grid, 256, smem, s>>>(r, row_sums); break;
+    default: set_smem(jsd_sweep_kernel<float>, (uint32_t)smem); jsd_sweep_kernel<float><<<grid, 256, smem, s>>>(r, row_sums); break;
+  }
+  return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
+}
+
+int32_t orda_shard_backward(const orda_distill_args_t* args, void* workspace, size_t workspace_bytes,
+                            const float* row_stats, const float* row_sums, void* stream) {
+  int rc = check_args(args);
+  if (rc) return rc;
+  const Plan P = make_plan(args, args->n_rows);
+  if ((rc = check_operands(args, P))) return rc;
+  if (!workspace || workspace_bytes < P.total || !row_stats) return ORDA_ERR_WORKSPACE;
+  if (P.jsd && !row_sums) return ORDA_ERR_INVALID_ARGUMENT;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const ChunkPtrs c = chunk_ptrs(args, 0, args->n_rows);
+  switch (args->compute_dtype) {
+    case ORDA_BF16:
+      rc = row_phases<__nv_bfloat16>(args, P, ws, c, s, false, true, row_stats, row_sums);
+      if (!rc) rc = grad_gemms<__nv_bfloat16>(args, P, ws, c, true, s);
+      break;
+    case ORDA_F16:
+      rc = row_phases<__half>(args, P, ws, c, s, false, true, row_stats, row_sums);
+      if (!rc) rc = grad_gemms<__half>(args, P, ws, c, true, s);
+      break;
+    default:
+      rc = row_phases<float>(args, P, ws, c, s, false, true, row_stats, row_sums);
+      if (!rc) rc = grad_gemms<float>(args, P, ws, c, true, s);
+      break;
+  }
+  if (rc) return rc;
+  const float* rl = args->out_row_losses ? args->out_row_losses : reinterpret_cast<const float*>(ws + P.off_row_losses);
+  finalize_kernel<<<1, 1024, 0, s>>>(rl, args->n_rows, args->labels, args->n_rows, args->ignore_index,
+                                     args->reduction, P.flags, args->student_ce_weight, args->teacher_ce_weight,
+                                     args->kl_weight, args->out_reduced);
+  return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
+}
+
+// ---------------------------------------------------------------- testing hook
+int32_t orda_debug_gemm(int32_t dtype, int32_t a_mn, int32_t b_mn, const void* A, int64_t lda, const void* B,
+                        int64_t ldb, int64_t M, int64_t N, int64_t K, float* out, int64_t ldo, int32_t* status,
+                        void* stream) {
+  if (dtype != ORDA_BF16 && dtype != ORDA_F16) return ORDA_ERR_INVALID_ARGUMENT;
+  TcGemmParams prm{};
+  prm.status = status;
+  int rc;
+  if ((rc = make_operand_map(&prm.a0, dtype, A, a_mn != 0, M, K, lda, kTileRows))) return rc;
+  if ((rc = make_operand_map(&prm.b0, dtype, B, b_mn != 0, N, K, ldb, 256))) return rc;
+  prm.kb0 = static_cast<int32_t>(cdiv(K, kBK));
+  prm.st = StoreEpiParams{out, ldo, M, N, 1, 0};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define ORDA_DBG(T, AM, BM) return launch_tc<256, AM, BM, GM_SINGLE, EPI_STORE, T>(prm, M, N, s, 8)
+  if (dtype == ORDA_BF16) {
+    if (a_mn && b_mn) ORDA_DBG(__nv_bfloat16, true, true);
+    if (a_mn) ORDA_DBG(__nv_bfloat16, true, false);
+    if (b_mn) ORDA_DBG(__nv_bfloat16, false, true);
+    ORDA_DBG(__nv_bfloat16, false, false);
+  }
+  if (a_mn && b_mn) ORDA_DBG(__half, true, true);
+  if (a_mn) ORDA_DBG(__half, true, false);
+  if (b_mn) ORDA_DBG(__half, false, true);
+  ORDA_DBG(__half, false, false);
+#undef ORDA_DBG
+}
+
+}  // extern "C"

@@ -1,0 +1,405 @@
+"""Parity of the CUDA path (public API -> C ABI -> sm_100a kernels) against the CPU oracle.
+
+Cases follow the reference's GPU tests (test/correctness/test_public_api_cuda.py: fp16, BT=16,
+H=32 / Ht=48, V=257, chunk_size=7, kl 0.35, T=1.4, 5 teacher modes, mean/sum, kl=0, T=1,
+non-contiguous inputs, tied teacher_ce=0) with the reference's tolerances (loss 5e-3, grads 5e-2),
+plus every divergence variant and BASELINE-shaped slices in bf16 at the target tolerances
+(loss 1e-3 relative, gradients 2e-2 relative) and fp32 at 1e-5.
+"""
+from __future__ import annotations
+
+import ast
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.distill_oracle import distill_reference
+
+pytestmark = pytest.mark.gpu
+
+ok = pytest.importorskip("orda_ce_kernel")
+from orda_ce_kernel import KernelConfig, PrecomputedTeacher, SeparateTeacher, TiedTeacher, distillation_loss  # noqa: E402
+
+MODES = ["tied", "separate", "separate-full", "precomputed-logits", "precomputed-hidden"]
+
+
+def _np(t):
+    return None if t is None else t.detach().double().cpu().numpy()
+
+
+def _make(mode, *, dtype, seed, BT=16, H=32, Ht=48, V=257, scale=0.1, ignore_every=4, w_scale=None):
+    """Inputs like the reference's factories: randn * 0.1, every BT//4-th label ignored."""
+    g = torch.Generator().manual_seed(seed)
+    w_scale = scale if w_scale is None else w_scale
+    hs = (torch.randn(BT, H, generator=g) * scale).to(dtype).cuda().requires_grad_(True)
+    weight = (torch.randn(V, H, generator=g) * w_scale).to(dtype).cuda().requires_grad_(True)
+    labels = torch.randint(0, V, (BT,), generator=g)
+    if ignore_every and BT >= ignore_every:
+        labels[:: BT // ignore_every] = -100
+    labels = labels.cuda()
+    tce = None
+    kw = {}
+    if mode == "tied":
+        ht = (torch.randn(BT, H, generator=g) * scale).to(dtype).cuda().requires_grad_(True)
+        teacher = TiedTeacher(ht)
+        kw = dict(mode="tied", teacher_hidden=ht)
+    elif mode in ("separate", "separate-full"):
+        full = mode == "separate-full"
+        ht = (torch.randn(BT, Ht, generator=g) * scale).to(dtype).cuda().requires_grad_(full)
+        wt = (torch.randn(V, Ht, generator=g) * w_scale).to(dtype).cuda().requires_grad_(full)
+        tce = 1.0 if full else None
+        teacher = SeparateTeacher(ht, wt)
+        kw = dict(mode="separate", teacher_hidden=ht, teacher_weight=wt)
+    elif mode == "precomputed-logits":
+        tl = (torch.randn(BT, V, generator=g) * scale).to(dtype).cuda()
+        teacher = PrecomputedTeacher(logits=tl)
+        kw = dict(mode="precomputed", teacher_logits=tl)
+    else:
+        ht = (torch.randn(BT, Ht, generator=g) * scale).to(dtype).cuda()
+        wt = (torch.randn(V, Ht, generator=g) * w_scale).to(dtype).cuda()
+        teacher = PrecomputedTeacher(teacher_hidden=ht, teacher_weight=wt)
+        kw = dict(mode="precomputed", teacher_hidden=ht, teacher_weight=wt)
+    return hs, weight, labels, teacher, tce, kw
+
+
+def _oracle(hs, weight, labels, kw, **loss_kw):
+    okw = {k: (_np(v) if isinstance(v, torch.Tensor) else v) for k, v in kw.items()}
+    return distill_reference(_np(hs), _np(weight), labels.cpu().numpy(), **okw, **loss_kw)
+
+
+def _close(actual, expected, *, atol, rtol, name):
+    a = float(actual)
+    assert abs(a - expected) <= atol + rtol * abs(expected), f"{name}: got {a:.8g} expected {expected:.8g}"
+
+
+def _grad_close(t, ref, *, atol, rtol, name):
+    assert t is not None, f"{name}: missing gradient"
+    np.testing.assert_allclose(t.detach().double().cpu().numpy(), ref, atol=atol, rtol=rtol, err_msg=name)
+
+
+def _rel_err(t, ref):
+    a = t.detach().double().cpu().numpy()
+    return float(np.linalg.norm(a - ref) / max(np.linalg.norm(ref), 1e-30))
+
+
+def _check_all(out, hs, weight, mode, teacher, tce, ref, *, atol_l, rtol_l, atol_g, rtol_g):
+    _close(out.loss, ref.loss, atol=atol_l, rtol=rtol_l, name="loss")
+    _close(out.student_ce, ref.student_ce, atol=atol_l, rtol=rtol_l, name="student_ce")
+    _close(out.teacher_ce, ref.teacher_ce, atol=atol_l, rtol=rtol_l, name="teacher_ce")
+    _close(out.kl, ref.kl, atol=atol_l, rtol=rtol_l, name="kl")
+    _grad_close(hs.grad, ref.d_student_hidden, atol=atol_g, rtol=rtol_g, name="student_hidden")
+    _grad_close(weight.grad, ref.d_weight, atol=atol_g, rtol=rtol_g, name="weight")
+    if mode == "tied":
+        _grad_close(teacher.hidden.grad, ref.d_teacher_hidden, atol=atol_g, rtol=rtol_g, name="teacher_hidden")
+    if mode == "separate-full":
+        _grad_close(teacher.hidden.grad, ref.d_teacher_hidden, atol=atol_g, rtol=rtol_g, name="teacher_hidden")
+        _grad_close(teacher.weight.grad, ref.d_teacher_weight, atol=atol_g, rtol=rtol_g, name="teacher_weight")
+    if mode == "separate":
+        assert teacher.hidden.grad is None and teacher.weight.grad is None
+
+
+# ----------------------------------------------------------------- ports of the reference GPU tests
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("reduction", ["mean", "sum"])
+def test_public_backend_matches_oracle(mode, reduction):
+    hs, weight, labels, teacher, tce, kw = _make(mode, dtype=torch.float16, seed=201)
+    out = distillation_loss(hs, weight, labels, teacher, teacher_ce_weight=tce, kl_weight=0.35,
+                            kl_temperature=1.4, reduction=reduction, backend="triton",
+                            config=KernelConfig(chunk_size=7))
+    out.loss.backward()
+    ref = _oracle(hs, weight, labels, kw, teacher_ce_weight=tce, kl_weight=0.35, kl_temperature=1.4,
+                  reduction=reduction)
+    _check_all(out, hs, weight, mode, teacher, tce, ref, atol_l=5e-3, rtol_l=5e-3, atol_g=5e-2, rtol_g=5e-2)
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_kl_weight_zero_gives_exact_zero_kl(mode):
+    hs, weight, labels, teacher, tce, kw = _make(mode, dtype=torch.float16, seed=401)
+    out = distillation_loss(hs, weight, labels, teacher, teacher_ce_weight=tce, kl_weight=0.0,
+                            kl_temperature=1.4, config=KernelConfig(chunk_size=7))
+    out.loss.backward()
+    ref = _oracle(hs, weight, labels, kw, teacher_ce_weight=tce, kl_weight=0.0, kl_temperature=1.4)
+    assert float(out.kl) == 0.0
+    _check_all(out, hs, weight, mode, teacher, tce, ref, atol_l=5e-3, rtol_l=5e-3, atol_g=5e-2, rtol_g=5e-2)
+
+
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("max_fused_size", [128, 512])
+def test_temperature_one(mode, max_fused_size):
+    hs, weight, labels, teacher, tce, kw = _make(mode, dtype=torch.float16, seed=501 + max_fused_size)
+    out = distillation_loss(hs, weight, labels, teacher, teacher_ce_weight=tce, kl_weight=0.35,
+                            kl_temperature=1.0, config=KernelConfig(chunk_size=7, max_fused_size=max_fused_size))
+    out.loss.backward()
+    ref = _oracle(hs, weight, labels, kw, teacher_ce_weight=tce, kl_weight=0.35, kl_temperature=1.0)
+    _check_all(out, hs, weight, mode, teacher, tce, ref, atol_l=5e-3, rtol_l=5e-3, atol_g=5e-2, rtol_g=5e-2)
+
+
+def test_tied_teacher_ce_zero_keeps_teacher_grad_zero():
+    hs, weight, labels, teacher, _tce, _kw = _make("tied", dtype=torch.float16, seed=601)
+    out = distillation_loss(hs, weight, labels, teacher, teacher_ce_weight=0.0, kl_weight=0.35,
+                            kl_temperature=1.4, config=KernelConfig(chunk_size=7))
+    out.loss.backward()
+    assert teacher.hidden.grad is not None
+    assert torch.count_nonzero(teacher.hidden.grad).item() == 0
+    assert float(out.teacher_ce) == 0.0
+
+
+def _noncontig(shape, seed, dtype=torch.float16, requires_grad=False):
+    g = torch.Generator().manual_seed(seed)
+    base = torch.randn(shape[1], shape[0], generator=g).to(dtype).cuda()
+    t = base.t()
+    assert not t.is_contiguous()
+    return t.requires_grad_(requires_grad)
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_noncontiguous_inputs(mode):
+    BT, Hs, Ht, V = 16, 32, 48, 257
+    g = torch.Generator().manual_seed(7)
+    labels = torch.randint(0, V, (BT,), generator=g)
+    labels[::4] = -100
+    labels = labels.cuda()
+    hs = _noncontig((BT, Hs), 301, requires_grad=True)
+    weight = _noncontig((V, Hs), 302, requires_grad=True)
+    tce = None
+    if mode == "tied":
+        ht = _noncontig((BT, Hs), 303, requires_grad=True)
+        teacher, kw = TiedTeacher(ht), dict(mode="tied", teacher_hidden=ht)
+    elif mode in ("separate", "separate-full"):
+        full = mode == "separate-full"
+        ht = _noncontig((BT, Ht), 304, requires_grad=full)
+        wt = _noncontig((V, Ht), 305, requires_grad=full)
+        tce = 1.0 if full else None
+        teacher, kw = SeparateTeacher(ht, wt), dict(mode="separate", teacher_hidden=ht, teacher_weight=wt)
+    elif mode == "precomputed-logits":
+        tl = _noncontig((BT, V), 306)
+        teacher, kw = PrecomputedTeacher(logits=tl), dict(mode="precomputed", teacher_logits=tl)
+    else:
+        ht = _noncontig((BT, Ht), 307)
+        wt = _noncontig((V, Ht), 308)
+        teacher = PrecomputedTeacher(teacher_hidden=ht, teacher_weight=wt)
+        kw = dict(mode="precomputed", teacher_hidden=ht, teacher_weight=wt)
+    out = distillation_loss(hs, weight, labels, teacher, teacher_ce_weight=tce, kl_weight=0.35,
+                            kl_temperature=1.4, config=KernelConfig(chunk_size=7))
+    out.loss.backward()
+    ref = _oracle(hs, weight, labels, kw, teacher_ce_weight=tce, kl_weight=0.35, kl_temperature=1.4)
+    _check_all(out, hs, weight, mode, teacher, tce, ref, atol_l=5e-3, rtol_l=5e-3, atol_g=5e-2, rtol_g=5e-2)
+
+
+# ----------------------------------------------------------------- golden fixtures through the fp32 path
+GOLDEN = sorted(glob.glob(os.path.join(os.path.dirname(__file__), "golden", "*.npz")))
+
+
+@pytest.mark.parametrize("path", GOLDEN, ids=[os.path.basename(p)[:-4] for p in GOLDEN])
+def test_golden_fixture_fp32_path(path):
+    d = np.load(path)
+    meta = ast.literal_eval(str(d["meta"]))
+    mode = meta.pop("mode")
+    f = lambda k, g=False: torch.tensor(d[k], dtype=torch.float32, device="cuda").requires_grad_(g)  # noqa: E731
+    hs, w = f("in_student_hidden", True), f("in_weight", True)
+    labels = torch.tensor(d["in_labels"], device="cuda")
+    ht = wt = None
+    if mode == "tied":
+        ht = f("in_teacher_hidden", True)
+        teacher = TiedTeacher(ht)
+    elif mode == "separate":
+        full = meta.get("teacher_ce_weight") not in (None, 0.0)
+        ht, wt = f("in_teacher_hidden", full), f("in_teacher_weight", full)
+        teacher = SeparateTeacher(ht, wt)
+    elif mode == "precomputed_logits":
+        teacher = PrecomputedTeacher(logits=f("in_teacher_logits"))
+    else:
+        teacher = PrecomputedTeacher(teacher_hidden=f("in_teacher_hidden"), teacher_weight=f("in_teacher_weight"))
+    out = distillation_loss(hs, w, labels, teacher, **meta)
+    out.loss.backward()
+    tol = dict(rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(float(out.loss), d["out_loss"], **tol)
+    np.testing.assert_allclose(float(out.student_ce), d["out_student_ce"], **tol)
+    np.testing.assert_allclose(float(out.teacher_ce), d["out_teacher_ce"], **tol)
+    np.testing.assert_allclose(float(out.kl), d["out_kl"], **tol)
+    np.testing.assert_allclose(hs.grad.double().cpu().numpy(), d["grad_student_hidden"], rtol=1e-4, atol=1e-6)
+    np.testing.assert_allclose(w.grad.double().cpu().numpy(), d["grad_weight"], rtol=1e-4, atol=1e-6)
+    if "grad_teacher_hidden" in d:
+        np.testing.assert_allclose(ht.grad.double().cpu().numpy(), d["grad_teacher_hidden"], rtol=1e-4, atol=1e-6)
+    if "grad_teacher_weight" in d:
+        np.testing.assert_allclose(wt.grad.double().cpu().numpy(), d["grad_teacher_weight"], rtol=1e-4, atol=1e-6)
+
+
+# ----------------------------------------------------------------- divergence variants (bf16, tensor cores)
+VARIANTS = [("forward", 0.5), ("reverse", 0.5), ("jsd", 0.5), ("jsd", 0.2), ("jsd", 0.0), ("jsd", 1.0)]
+
+
+def _llm_inputs(mode, seed, BT=300, H=256, Ht=384, V=3000):
+    """BASELINE-style distributions: hidden ~ N(0,1), lm_head ~ N(0, 0.02), labels with ignored rows."""
+    return _make(mode, dtype=torch.bfloat16, seed=seed, BT=BT, H=H, Ht=Ht, V=V, scale=1.0, w_scale=0.02,
+                 ignore_every=20)
+
+
+@pytest.mark.parametrize("mode", ["tied", "separate", "separate-full", "precomputed-logits", "precomputed-hidden"])
+@pytest.mark.parametrize("div,beta", VARIANTS)
+@pytest.mark.parametrize("temperature", [1.0, 1.5])
+def test_divergence_variants_bf16(mode, div, beta, temperature):
+    hs, weight, labels, teacher, tce, kw = _llm_inputs(mode, seed=11)
+    if mode == "precomputed-logits":
+        # teacher logits ~ N(0, 2) given as fp32 log-softmax
+        g = torch.Generator().manual_seed(12)
+        tl = torch.log_softmax(torch.randn(*labels.shape, weight.shape[0], generator=g) * 2.0, -1).cuda()
+        teacher = PrecomputedTeacher(logits=tl)
+        kw = dict(mode="precomputed", teacher_logits=tl)
+    out = distillation_loss(hs, weight, labels, teacher, teacher_ce_weight=tce, student_ce_weight=0.5,
+                            kl_weight=0.5, kl_temperature=temperature, kl_divergence=div, jsd_beta=beta)
+    out.loss.backward()
+    ref = _oracle(hs, weight, labels, kw, teacher_ce_weight=tce, student_ce_weight=0.5, kl_weight=0.5,
+                  kl_temperature=temperature, kl_divergence=div, jsd_beta=beta)
+    _close(out.loss, ref.loss, atol=0.0, rtol=1e-3, name="loss")
+    _close(out.kl, ref.kl, atol=1e-5, rtol=1e-3, name="kl")
+    assert _rel_err(hs.grad, ref.d_student_hidden) < 2e-2
+    assert _rel_err(weight.grad, ref.d_weight) < 2e-2
+    if mode == "separate-full":
+        assert _rel_err(teacher.hidden.grad, ref.d_teacher_hidden) < 2e-2
+        assert _rel_err(teacher.weight.grad, ref.d_teacher_weight) < 2e-2
+
+
+# ----------------------------------------------------------------- BASELINE config 1 (fp32, full size)
+def test_config1_fp32_student_only():
+    from oracle.distill_oracle import synthetic_case
+
+    c = synthetic_case(n=512, h=256, v=4096, seed=0, ignore_frac=0.05)
+    hs = torch.tensor(c["student_hidden"], device="cuda", requires_grad=True)
+    w = torch.tensor(c["weight"], device="cuda", requires_grad=True)
+    labels = torch.tensor(c["labels"], device="cuda")
+    out = distillation_loss(hs, w, labels, TiedTeacher(hs.detach()), teacher_ce_weight=0.0, kl_weight=0.0)
+    out.loss.backward()
+    ref = distill_reference(c["student_hidden"], c["weight"], c["labels"], mode="tied",
+                            teacher_hidden=c["student_hidden"], teacher_ce_weight=0.0, kl_weight=0.0)
+    _close(out.loss, ref.loss, atol=0.0, rtol=1e-5, name="loss")
+    np.testing.assert_allclose(hs.grad.double().cpu().numpy(), ref.d_student_hidden, rtol=1e-4, atol=1e-8)
+    np.testing.assert_allclose(w.grad.double().cpu().numpy(), ref.d_weight, rtol=1e-4, atol=1e-8)
+
+
+# ----------------------------------------------------------------- edge cases
+def test_single_row_and_all_ignored():
+    hs, weight, labels, teacher, tce, kw = _llm_inputs("tied", seed=21, BT=1, V=1000)
+    out = distillation_loss(hs, weight, labels, teacher, kl_weight=0.3)
+    out.loss.backward()
+    ref = _oracle(hs, weight, labels, kw, kl_weight=0.3)
+    _close(out.loss, ref.loss, atol=1e-6, rtol=1e-3, name="loss")
+
+    hs, weight, labels, teacher, tce, kw = _llm_inputs("tied", seed=22, BT=130, V=1000)
+    labels = torch.full_like(labels, -100)
+    out = distillation_loss(hs, weight, labels, teacher, kl_weight=0.3)
+    out.loss.backward()
+    for v in out:
+        assert float(v) == 0.0
+    assert torch.count_nonzero(hs.grad).item() == 0
+    assert torch.count_nonzero(weight.grad).item() == 0
+
+
+def test_out_of_range_label_reads_as_zero():
+    """Reference row-kernel semantics (ops/tied_teacher.py:42-44): a non-ignored label outside
+    [0, V) is read as label 0 when labels are not validated."""
+    hs, weight, labels, teacher, tce, kw = _llm_inputs("tied", seed=23, BT=64, V=777)
+    labels = labels.clone()
+    labels[5] = 5000
+    labels[9] = -7
+    out = distillation_loss(hs, weight, labels, teacher, kl_weight=0.3)
+    out.loss.backward()
+    fixed = labels.clone()
+    fixed[5] = 0
+    fixed[9] = 0
+    ref = _oracle(hs, weight, fixed, kw, kl_weight=0.3)
+    _close(out.loss, ref.loss, atol=0.0, rtol=1e-3, name="loss")
+    assert _rel_err(hs.grad, ref.d_student_hidden) < 2e-2
+    with pytest.raises(ValueError, match="labels contains values outside"):
+        distillation_loss(hs, weight, labels, teacher, kl_weight=0.3, profile="debug")
+
+
+def test_hidden_not_multiple_of_8_is_padded():
+    hs, weight, labels, teacher, tce, kw = _make("tied", dtype=torch.bfloat16, seed=31, BT=40, H=36, V=500,
+                                                 scale=1.0, w_scale=0.05)
+    out = distillation_loss(hs, weight, labels, teacher, kl_weight=0.4, kl_temperature=2.0)
+    out.loss.backward()
+    ref = _oracle(hs, weight, labels, kw, kl_weight=0.4, kl_temperature=2.0)
+    _close(out.loss, ref.loss, atol=0.0, rtol=1e-3, name="loss")
+    assert hs.grad.shape == hs.shape and weight.grad.shape == weight.shape
+    assert _rel_err(hs.grad, ref.d_student_hidden) < 2e-2
+    assert _rel_err(weight.grad, ref.d_weight) < 2e-2
+
+
+@pytest.mark.parametrize("mode", ["tied", "separate-full", "precomputed-logits"])
+def test_chunking_does_not_change_results(mode):
+    hs, weight, labels, teacher, tce, kw = _llm_inputs(mode, seed=41, BT=700, V=2000)
+    outs = []
+    for cfg in (KernelConfig(), KernelConfig(chunk_size=128), KernelConfig(num_chunks=3)):
+        for t in (hs, weight):
+            t.grad = None
+        o = distillation_loss(hs, weight, labels, teacher, teacher_ce_weight=tce, kl_weight=0.5, config=cfg)
+        o.loss.backward()
+        outs.append((float(o.loss), hs.grad.float().clone(), weight.grad.float().clone()))
+    for loss, gh, gw in outs[1:]:
+        assert abs(loss - outs[0][0]) <= 1e-5 * abs(outs[0][0])
+        torch.testing.assert_close(gh, outs[0][1], rtol=0, atol=0)  # rows are independent: bitwise equal
+        torch.testing.assert_close(gw, outs[0][2], rtol=2e-2, atol=1e-4)  # bf16 accumulation across chunks
+
+
+def test_fp32_weight_accumulation_debug_profile():
+    hs, weight, labels, teacher, tce, kw = _llm_inputs("tied", seed=51, BT=500, V=1500)
+    out = distillation_loss(hs, weight, labels, teacher, kl_weight=0.5, profile="debug",
+                            config=KernelConfig(chunk_size=128))
+    out.loss.backward()
+    ref = _oracle(hs, weight, labels, kw, kl_weight=0.5)
+    _close(out.loss, ref.loss, atol=0.0, rtol=1e-3, name="loss")
+    assert _rel_err(weight.grad, ref.d_weight) < 2e-2
+
+
+def test_module_matches_functional_and_repeat_is_deterministic():
+    hs, weight, labels, teacher, tce, kw = _llm_inputs("tied", seed=61, BT=256, V=1500)
+    mod = ok.DistillationLoss(kl_weight=0.25, kl_temperature=1.3)
+    a = mod(hs, weight, labels, teacher)
+    b = distillation_loss(hs, weight, labels, teacher, kl_weight=0.25, kl_temperature=1.3)
+    for x, y in zip(a, b):
+        assert float(x) == float(y)
+
+
+# ----------------------------------------------------------------- BASELINE-shaped slices (bf16)
+def test_config2_precomputed_slice():
+    from oracle.distill_oracle import synthetic_case
+
+    c = synthetic_case(n=256, h=2048, v=32000, seed=2, ignore_frac=0.05, teacher_logit_std=2.0)
+    hs = torch.tensor(c["student_hidden"]).to(torch.bfloat16).cuda().requires_grad_(True)
+    w = torch.tensor(c["weight"]).to(torch.bfloat16).cuda().requires_grad_(True)
+    labels = torch.tensor(c["labels"]).cuda()
+    tl = torch.tensor(c["teacher_logits"]).cuda()
+    out = distillation_loss(hs, w, labels, PrecomputedTeacher(logits=tl), student_ce_weight=0.5, kl_weight=0.5,
+                            kl_temperature=2.0)
+    out.loss.backward()
+    ref = distill_reference(_np(hs), _np(w), c["labels"], mode="precomputed", teacher_logits=c["teacher_logits"],
+                            student_ce_weight=0.5, kl_weight=0.5, kl_temperature=2.0)
+    _close(out.loss, ref.loss, atol=0.0, rtol=1e-3, name="loss")
+    assert _rel_err(hs.grad, ref.d_student_hidden) < 2e-2
+    assert _rel_err(w.grad, ref.d_weight) < 2e-2
+
+
+@pytest.mark.parametrize("div", ["forward", "reverse", "jsd"])
+def test_config3_llama_shape_slice(div):
+    """Llama-3-8B head (H=4096, V=128256), tied teacher, 64-row slice of BASELINE config 3."""
+    from oracle.distill_oracle import synthetic_case
+
+    c = synthetic_case(n=64, h=4096, v=128256, seed=3, ignore_frac=0.05)
+    g = np.random.default_rng(33)
+    ht_np = g.standard_normal((64, 4096), dtype=np.float32)
+    hs = torch.tensor(c["student_hidden"]).to(torch.bfloat16).cuda().requires_grad_(True)
+    ht = torch.tensor(ht_np).to(torch.bfloat16).cuda()
+    w = torch.tensor(c["weight"]).to(torch.bfloat16).cuda().requires_grad_(True)
+    labels = torch.tensor(c["labels"]).cuda()
+    out = distillation_loss(hs, w, labels, TiedTeacher(ht), kl_weight=1.0, kl_temperature=1.0, kl_divergence=div)
+    out.loss.backward()
+    ref = distill_reference(_np(hs), _np(w), c["labels"], mode="tied", teacher_hidden=_np(ht), kl_weight=1.0,
+                            kl_temperature=1.0, kl_divergence=div, need_teacher_hidden_grad=False)
+    _close(out.loss, ref.loss, atol=0.0, rtol=1e-3, name="loss")
+    _close(out.kl, ref.kl, atol=0.0, rtol=1e-3, name="kl")
+    assert _rel_err(hs.grad, ref.d_student_hidden) < 2e-2
+    assert _rel_err(w.grad, ref.d_weight) < 2e-2
