@@ -125,7 +125,22 @@ typedef struct orda_distill_args {
   void* grad_teacher_weight;    /* [vocab, teacher_hidden], compute dtype or fp32                    */
   int32_t grad_weight_fp32;     /* grad_weight / grad_teacher_weight are fp32 accumulators            */
   int32_t* device_status;       /* int32 device word, zero on entry                                   */
+
+  /* optional instrumentation / overlap hooks (host handles; NULL = off) */
+  void* const* phase_events;    /* 2*ORDA_PHASES cudaEvent_t: start/end recorded around each phase of
+                                   the LAST chunk (timing of the individual kernels)                  */
+  void* dweight_done_event;     /* cudaEvent_t recorded once the weight gradients are complete, so a
+                                   caller can start their all-reduce on another stream                 */
+  int32_t dweight_first;        /* run the dW GEMMs before the dH GEMMs (overlap the dW all-reduce)  */
+  int32_t reserved0;
 } orda_distill_args_t;
+
+/* phases bracketed by phase_events */
+#define ORDA_PHASE_LOGITS 0     /* logits GEMM(s) + statistics epilogue                              */
+#define ORDA_PHASE_ROWS 1       /* row merge, losses, (JSD sweep), dlogits sweep                     */
+#define ORDA_PHASE_DHIDDEN 2    /* dHidden GEMM(s)                                                    */
+#define ORDA_PHASE_DWEIGHT 3    /* dWeight GEMM(s)                                                    */
+#define ORDA_PHASES 4
 
 /* Version of this ABI (ORDA_ABI_VERSION). */
 int32_t orda_abi_version(void);

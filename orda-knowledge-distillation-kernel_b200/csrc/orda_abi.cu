@@ -357,9 +357,20 @@ int row_phases(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const C
   return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
 }
 
+// Records the start / end event of a phase (instrumentation hook; no-op without events).
+struct PhaseMark {
+  const orda_distill_args_t* a;
+  cudaStream_t s;
+  bool on;
+  void mark(int phase, int end) const {
+    if (on && a->phase_events && a->phase_events[2 * phase + end])
+      cudaEventRecord(static_cast<cudaEvent_t>(a->phase_events[2 * phase + end]), s);
+  }
+};
+
 template <typename WsT>
 int grad_gemms(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const ChunkPtrs& c, bool first_chunk,
-               cudaStream_t s) {
+               cudaStream_t s, const PhaseMark* pm = nullptr, bool last_chunk = true) {
   const bool tied = a->teacher_mode == ORDA_TEACHER_TIED;
   const bool sep = a->teacher_mode == ORDA_TEACHER_SEPARATE;
   void* ws_s = ws + P.off_ws_s;
@@ -391,26 +402,47 @@ int grad_gemms(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const C
       simt_gemm(zt, 1, P.vpad, reinterpret_cast<const float*>(c.ht), 1, a->ld_teacher_hidden,
                 static_cast<float*>(a->grad_teacher_weight), a->teacher_hidden, a->vocab, a->teacher_hidden, c.rows,
                 acc, s);
+    if (last_chunk && a->dweight_done_event) cudaEventRecord(static_cast<cudaEvent_t>(a->dweight_done_event), s);
     rc = cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
   } else {
     int32_t* st = a->device_status;
-    if (a->need_grad_student_hidden)
-      if ((rc = dh_tc<WsT>(a, P, ws_s, a->weight, a->ld_weight, a->hidden, c.grad_hs, c.rows, st, s))) return rc;
-    if (a->need_grad_weight) {
-      const bool two = tied && P.grad_t;
-      if ((rc = dw_tc<WsT>(a, P, ws_s, c.hs, a->ld_student_hidden, two ? ws_t : nullptr, two ? c.ht : nullptr,
-                           a->ld_teacher_hidden, a->hidden, a->grad_weight, a->grad_weight_fp32, acc, c.rows, st, s)))
-        return rc;
+    auto dhidden = [&]() -> int {
+      int r = ORDA_OK;
+      if (pm) pm->mark(ORDA_PHASE_DHIDDEN, 0);
+      if (a->need_grad_student_hidden)
+        if ((r = dh_tc<WsT>(a, P, ws_s, a->weight, a->ld_weight, a->hidden, c.grad_hs, c.rows, st, s))) return r;
+      if (P.grad_t && a->need_grad_teacher_hidden) {
+        const void* wm = tied ? a->weight : a->teacher_weight;
+        const int64_t ldm = tied ? a->ld_weight : a->ld_teacher_weight;
+        if ((r = dh_tc<WsT>(a, P, ws_t, wm, ldm, a->teacher_hidden, c.grad_ht, c.rows, st, s))) return r;
+      }
+      if (pm) pm->mark(ORDA_PHASE_DHIDDEN, 1);
+      return r;
+    };
+    auto dweight = [&]() -> int {
+      int r = ORDA_OK;
+      if (pm) pm->mark(ORDA_PHASE_DWEIGHT, 0);
+      if (a->need_grad_weight) {
+        const bool two = tied && P.grad_t;
+        if ((r = dw_tc<WsT>(a, P, ws_s, c.hs, a->ld_student_hidden, two ? ws_t : nullptr, two ? c.ht : nullptr,
+                            a->ld_teacher_hidden, a->hidden, a->grad_weight, a->grad_weight_fp32, acc, c.rows, st, s)))
+          return r;
+      }
+      if (sep && P.grad_t && a->need_grad_teacher_weight)
+        if ((r = dw_tc<WsT>(a, P, ws_t, c.ht, a->ld_teacher_hidden, nullptr, nullptr, 0, a->teacher_hidden,
+                            a->grad_teacher_weight, a->grad_weight_fp32, acc, c.rows, st, s)))
+          return r;
+      if (pm) pm->mark(ORDA_PHASE_DWEIGHT, 1);
+      if (last_chunk && a->dweight_done_event) cudaEventRecord(static_cast<cudaEvent_t>(a->dweight_done_event), s);
+      return r;
+    };
+    if (a->dweight_first) {
+      if ((rc = dweight())) return rc;
+      if ((rc = dhidden())) return rc;
+    } else {
+      if ((rc = dhidden())) return rc;
+      if ((rc = dweight())) return rc;
     }
-    if (P.grad_t && a->need_grad_teacher_hidden) {
-      const void* wm = tied ? a->weight : a->teacher_weight;
-      const int64_t ldm = tied ? a->ld_weight : a->ld_teacher_weight;
-      if ((rc = dh_tc<WsT>(a, P, ws_t, wm, ldm, a->teacher_hidden, c.grad_ht, c.rows, st, s))) return rc;
-    }
-    if (sep && P.grad_t && a->need_grad_teacher_weight)
-      if ((rc = dw_tc<WsT>(a, P, ws_t, c.ht, a->ld_teacher_hidden, nullptr, nullptr, 0, a->teacher_hidden,
-                           a->grad_teacher_weight, a->grad_weight_fp32, acc, c.rows, st, s)))
-        return rc;
   }
   // tied teacher with teacher CE off: the reference returns an all-zero teacher-hidden gradient
   if (tied && a->need_grad_teacher_hidden && !P.grad_t)
@@ -462,11 +494,16 @@ int run_all(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, cudaStream
   for (int64_t r0 = 0; r0 < a->n_rows; r0 += P.C) {
     const int64_t rows = std::min<int64_t>(P.C, a->n_rows - r0);
     const ChunkPtrs c = chunk_ptrs(a, r0, rows);
+    const PhaseMark pm{a, s, r0 + rows >= a->n_rows};
+    pm.mark(ORDA_PHASE_LOGITS, 0);
     if constexpr (std::is_same<WsT, float>::value) rc = forward_f32(a, P, ws, c, s);
     else rc = forward_tc<WsT>(a, P, ws, c, s);
     if (rc) return rc;
+    pm.mark(ORDA_PHASE_LOGITS, 1);
+    pm.mark(ORDA_PHASE_ROWS, 0);
     if ((rc = row_phases<WsT>(a, P, ws, c, s, true, true, nullptr, nullptr))) return rc;
-    if ((rc = grad_gemms<WsT>(a, P, ws, c, r0 == 0, s))) return rc;
+    pm.mark(ORDA_PHASE_ROWS, 1);
+    if ((rc = grad_gemms<WsT>(a, P, ws, c, r0 == 0, s, &pm, pm.on))) return rc;
   }
   const float* rl = a->out_row_losses ? a->out_row_losses : reinterpret_cast<const float*>(ws + P.off_row_losses);
   finalize_kernel<<<1, 1024, 0, s>>>(rl, a->n_rows, a->labels, a->n_rows, a->ignore_index, a->reduction, P.flags,

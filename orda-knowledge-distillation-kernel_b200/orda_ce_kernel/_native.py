@@ -37,6 +37,8 @@ OUT_LOSS, OUT_STUDENT_CE, OUT_TEACHER_CE, OUT_KL, OUT_MEAN_SCALE = 0, 1, 2, 3, 4
 OUT_SUM_STUDENT_CE, OUT_SUM_TEACHER_CE, OUT_SUM_KL, OUT_COUNT = 5, 6, 7, 8
 OUT_SLOTS = 9
 ROW_STATS = 16
+PHASE_LOGITS, PHASE_ROWS, PHASE_DHIDDEN, PHASE_DWEIGHT = 0, 1, 2, 3
+PHASES = 4
 
 _i32, _i64, _f32, _vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
 
@@ -67,6 +69,10 @@ class DistillArgs(ctypes.Structure):
         ("grad_teacher_hidden", _vp), ("grad_teacher_weight", _vp),
         ("grad_weight_fp32", _i32),
         ("device_status", _vp),
+        ("phase_events", _vp),
+        ("dweight_done_event", _vp),
+        ("dweight_first", _i32),
+        ("reserved0", _i32),
     ]
 
 
