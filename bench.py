@@ -1,0 +1,431 @@
+"""Benchmark of the fused CE + KL distillation loss (forward + backward) at the Llama-3-8B head shape.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--divergence forward]
+
+Workload: N=8192 tokens (batch 4 x seq 2048), hidden 4096, vocab 128256, bf16,
+tied teacher sharing the lm_head, forward KL at T=1 with weight 1.0, teacher CE weight 1.0 (the tied
+default), student hidden and lm_head take gradients, teacher hidden does not. Synthetic seeded inputs
+with BASELINE's distributions (hidden ~ N(0,1), lm_head ~ N(0, 0.02), 5% ignore_index labels).
+
+One step = ``distillation_loss(...)`` + ``loss.backward()``. ``value`` is whole-job tokens/s with the
+inputs resident in HBM (every input is larger than L2 or is re-read from HBM: the lm_head alone is
+1.05 GB); ``e2e`` is the same call with the step's hidden states and labels copied from pinned host
+memory and the loss read back each step. With N > 1 GPUs (torchrun) every rank runs its own 8192
+tokens (token-sharded data parallelism, weak scaling) and the lm_head gradient is all-reduced over
+NCCL, overlapped with the dHidden GEMM.
+
+``--impl reference`` times the reference's own PyTorch CPU implementation
+(``distillation_loss(..., backend="torch")`` from the installed reference package) on a 256-row
+slice of the same workload using all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(ROOT, "orda-knowledge-distillation-kernel_b200")
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+METRIC = "fused CE+KL fwd+bwd tokens/sec at Llama-3-8B shape; % bf16 tensor peak; 1/2/4/8 GPU"
+N_TOK, HID, VOCAB = 8192, 4096, 128256
+CPU_ROWS = 256
+
+
+def _args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--divergence", default="forward", choices=["forward", "reverse", "jsd"])
+    p.add_argument("--rows", type=int, default=N_TOK, help="tokens per GPU")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+def _dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def _workload(torch, rows, seed_offset, device):
+    g = torch.Generator(device="cpu").manual_seed(1000 + seed_offset)
+    hs = torch.randn(rows, HID, generator=g, dtype=torch.float32).to(torch.bfloat16)
+    g2 = torch.Generator(device="cpu").manual_seed(2000 + seed_offset)
+    ht = torch.randn(rows, HID, generator=g2, dtype=torch.float32).to(torch.bfloat16)
+    gw = torch.Generator(device="cpu").manual_seed(3000)
+    w = (torch.randn(VOCAB, HID, generator=gw, dtype=torch.float32) * 0.02).to(torch.bfloat16)
+    gl = torch.Generator(device="cpu").manual_seed(4000 + seed_offset)
+    labels = torch.randint(0, VOCAB, (rows,), generator=gl)
+    ign = torch.randperm(rows, generator=gl)[: rows // 20]
+    labels[ign] = -100
+    if device is None:
+        return hs, ht, w, labels
+    return hs.to(device), ht.to(device), w.to(device), labels.to(device)
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.samples = []
+        self._stop = threading.Event()
+        self._thr = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(
+                    ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits"],
+                    capture_output=True, text=True, timeout=5).stdout.strip()
+                if out:
+                    self.samples.append([x.strip() for x in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._thr = threading.Thread(target=self._run, daemon=True)
+        self._thr.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thr:
+            self._thr.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no nvidia-smi samples"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for s in self.samples:
+            for i, n in enumerate(names):
+                if len(s) > 5 + i and s[5 + i].lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.samples)}
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 1590.0, 6650.0, "fallback"
+
+
+def _profile_traffic():
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary (if present)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic_cfg3.json")) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+def _import_reference_package():
+    """The unmodified reference package installed in baseline/_ref, loaded under a private module
+    name so it cannot collide with this repository's ``orda_ce_kernel``."""
+    import importlib.util
+
+    pkg = os.path.join(REF_DIR, "orda_ce_kernel")
+    if not os.path.isfile(os.path.join(pkg, "__init__.py")):
+        return None
+    name = "_orda_reference_pkg"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, os.path.join(pkg, "__init__.py"),
+                                                  submodule_search_locations=[pkg])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _cpu_reference_rows(torch, rows, divergence):
+    """Times the reference's torch CPU path on `rows` rows of the workload; returns (tok/s, sample, kind)."""
+    hs, ht, w, labels = _workload(torch, N_TOK, 0, None)
+    hs, ht, labels = hs[:rows].clone(), ht[:rows].clone(), labels[:rows].clone()
+    ref = _import_reference_package() if divergence == "forward" else None
+    if ref is not None:
+
+        def run():
+            h = hs.clone().requires_grad_(True)
+            ww = w.clone().requires_grad_(True)
+            out = ref.distillation_loss(h, ww, labels, ref.TiedTeacher(ht), kl_weight=1.0, kl_temperature=1.0,
+                                        backend="torch")
+            out.loss.backward()
+            return float(out.loss)
+
+        kind = "reference"
+    else:
+        import numpy as np
+
+        sys.path.insert(0, ROOT)
+        from oracle.distill_oracle import distill_reference
+
+        hsn, htn, wn, ln = hs.float().numpy(), ht.float().numpy(), w.float().numpy(), labels.numpy()
+
+        def run():
+            return distill_reference(hsn, wn, ln, mode="tied", teacher_hidden=htn, kl_weight=1.0,
+                                     kl_temperature=1.0, kl_divergence=divergence).loss
+
+        kind = "port"
+    run()  # warm-up
+    times = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return rows / t, f"{rows} of {N_TOK} rows, H={HID}, V={VOCAB}, bf16, median of 3", kind
+
+
+def run_reference(args):
+    import torch
+
+    world, rank, _ = _dist_env()
+    if rank != 0:
+        return 0
+    threads = torch.get_num_threads()
+    hs, ht, w, labels = _workload(torch, N_TOK, 0, None)
+    hs, ht, labels = hs[:CPU_ROWS].clone(), ht[:CPU_ROWS].clone(), labels[:CPU_ROWS].clone()
+    ref = _import_reference_package()
+    if ref is None:
+        print(json.dumps({"impl": "reference", "unavailable": "reference package not installed in baseline/_ref"}))
+        return 0
+
+    def step():
+        h = hs.clone().requires_grad_(True)
+        ww = w.clone().requires_grad_(True)
+        out = ref.distillation_loss(h, ww, labels, ref.TiedTeacher(ht), kl_weight=1.0, kl_temperature=1.0,
+                                    backend="torch")
+        out.loss.backward()
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    value = CPU_ROWS * args.steps / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"config 3 row slice ({CPU_ROWS} of {N_TOK} tokens) on host CPU",
+                   "tokens": CPU_ROWS, "hidden": HID, "vocab": VOCAB, "teacher": "tied", "divergence": "forward",
+                   "temperature": 1.0},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                         "sample": f"{CPU_ROWS} rows x {args.steps} steps, reference torch path (backend='torch')"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def run_ours(args):
+    import torch
+
+    sys.path.insert(0, PKG_DIR)
+    sys.path.insert(0, ROOT)
+    import orda_ce_kernel as ok
+    from orda_ce_kernel import _fused, _native
+
+    world, rank, local = _dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev)
+        pg = dist.group.WORLD
+    if not ok.is_available():
+        raise RuntimeError("orda_ce_kernel CUDA kernels unavailable (B200 + built library required)")
+    lib = _native.load()
+
+    rows = args.rows
+    hs_h, ht_h, w_h, lab_h = _workload(torch, rows, rank, None)
+    w = w_h.to(dev).requires_grad_(True)
+    hs = hs_h.to(dev).requires_grad_(True)
+    ht = ht_h.to(dev)
+    labels = lab_h.to(dev)
+    teacher = ok.TiedTeacher(ht)
+    kw = dict(kl_weight=1.0, kl_temperature=1.0, kl_divergence=args.divergence)
+
+    comm_stream = torch.cuda.Stream(device=dev) if pg is not None else None
+
+    def primed(ev):
+        # the library records these events through their raw handles; recording each once here makes
+        # torch create the underlying CUDA event (torch only creates events lazily on first record)
+        ev.record()
+        return ev
+
+    done = primed(torch.cuda.Event()) if pg is not None else None
+
+    def step(h, t, lab, events=None):
+        h.grad = None
+        w.grad = None
+        with _fused.instrument(phase_events=events, dweight_done_event=done, dweight_first=pg is not None):
+            out = ok.distillation_loss(h, w, lab, ok.TiedTeacher(t), **kw)
+            out.loss.backward()
+        if pg is not None:
+            import torch.distributed as dist
+
+            # the lm_head gradient of the token shards is summed over the ranks (NCCL over NVLink),
+            # overlapped with the dHidden GEMM which runs after the dW GEMM on the main stream
+            comm_stream.wait_event(done)
+            with torch.cuda.stream(comm_stream):
+                dist.all_reduce(w.grad, group=pg)
+            torch.cuda.current_stream().wait_stream(comm_stream)
+        return out
+
+    def sync_all():
+        torch.cuda.synchronize()
+        if pg is not None:
+            import torch.distributed as dist
+
+            dist.barrier(group=pg)
+            torch.cuda.synchronize()
+
+    args.warmup = max(args.warmup, 3)  # at least three untimed warm-up steps
+    for _ in range(args.warmup):
+        step(hs, ht, labels)
+    sync_all()
+
+    # ---------------- device-resident timed region
+    K = args.steps
+    phase_ev = [[primed(torch.cuda.Event(enable_timing=True)) for _ in range(2 * _native.PHASES)] for _ in range(K)]
+    launches0 = lib.orda_kernel_launches()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        sync_all()
+        start.record()
+        for i in range(K):
+            out = step(hs, ht, labels, phase_ev[i])
+        end.record()
+        sync_all()
+    launches = lib.orda_kernel_launches() - launches0
+    ms = start.elapsed_time(end) / K
+    if pg is not None:
+        import torch.distributed as dist
+
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=pg)
+        ms = float(t.item())
+    value = world * rows / (ms / 1e3)
+
+    phase_ms = [statistics.mean(phase_ev[i][2 * p].elapsed_time(phase_ev[i][2 * p + 1]) for i in range(K))
+                for p in range(_native.PHASES)]
+    flops_tok = {0: 4.0 * HID * VOCAB, 2: 2.0 * HID * VOCAB, 3: 4.0 * HID * VOCAB}  # fwd (s+t), dH_s, dW (s+t)
+    names = {0: "logits GEMM + statistics epilogue (tc_gemm_kernel fwd)", 1: "row kernels",
+             2: "dHidden GEMM (tc_gemm_kernel)", 3: "dWeight GEMM (tc_gemm_kernel)"}
+    dom = max((0, 2, 3), key=lambda p: phase_ms[p])
+    peak_tf, peak_hbm, peak_src = _peaks()
+    achieved = flops_tok[dom] * rows / (phase_ms[dom] / 1e3) / 1e12
+    total_flops_tok = 10.0 * HID * VOCAB
+    step_tf = total_flops_tok * rows / (ms / 1e3) / 1e12
+    traffic = _profile_traffic().get(str(dom))
+
+    # ---------------- end-to-end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        hs_p, ht_p, lab_p = hs_h.pin_memory(), ht_h.pin_memory(), lab_h.pin_memory()
+        loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+        hs_d = torch.empty_like(hs_h, device=dev)
+        ht_d = torch.empty_like(ht_h, device=dev)
+        lab_d = torch.empty_like(lab_h, device=dev)
+
+        def e2e_step():
+            hs_d.copy_(hs_p, non_blocking=True)
+            ht_d.copy_(ht_p, non_blocking=True)
+            lab_d.copy_(lab_p, non_blocking=True)
+            o = step(hs_d.detach().requires_grad_(True), ht_d, lab_d)
+            loss_host.copy_(o.loss.detach(), non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        sync_all()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(K):
+            e2e_step()
+        e2.record()
+        sync_all()
+        ms_e2e = s2.elapsed_time(e2) / K
+        if pg is not None:
+            import torch.distributed as dist
+
+            t = torch.tensor([ms_e2e], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=pg)
+            ms_e2e = float(t.item())
+        e2e = {"value": world * rows / (ms_e2e / 1e3), "unit": "tokens/s",
+               "h2d_bytes_per_step": hs_h.numel() * 2 + ht_h.numel() * 2 + lab_h.numel() * 8,
+               "d2h_bytes_per_step": 4}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, sample, kind = _cpu_reference_rows(torch, CPU_ROWS, args.divergence)
+        cpu = {"value": v, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": kind, "sample": sample}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded; BASELINE config 3 distributions)",
+            "config": {
+                "workload": "config 3: tied teacher at the Llama-3-8B head, N=8192 tokens/GPU (4x2048), H=4096, "
+                            "V=128256, forward KL (T=1, weight 1), teacher CE 1.0, dHidden + dW",
+                "tokens_per_gpu": rows, "hidden": HID, "vocab": VOCAB, "divergence": args.divergence,
+                "parallelism": f"token-sharded dp{world}" if world > 1 else "single GPU",
+                "l2": "inputs larger than L2 (lm_head 1.05 GB, logits workspace 4.2 GB)",
+            },
+            "tflops_per_gpu": step_tf / world if world > 1 else step_tf,
+            "frac_of_bf16_peak_step": (step_tf / world) / peak_tf,
+            "phase_ms": {names[p]: phase_ms[p] for p in range(_native.PHASES)},
+            "roofline": {"bound": "tensor", "kernel": names[dom], "achieved": achieved, "peak": peak_tf,
+                         "unit": "TFLOP/s", "frac": achieved / peak_tf, "peak_source": peak_src,
+                         "traffic": traffic},
+            "gpu_launches": int(launches),
+            "clocks": clk.summary(),
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "loss": float(out.loss),
+        }
+        print(json.dumps(line))
+    if pg is not None:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = _args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

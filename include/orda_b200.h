@@ -22,7 +22,7 @@
  *     that timed out) are written to *device_status (int32, device memory, zero on entry); the
  *     caller reads it whenever it chooses. Kernels never trap.
  *   - Thread-safe and re-entrant: no global mutable state besides a per-process cache of the
- *     driver entry point used to encode TMA descriptors.
+ *     driver entry point used to encode TMA descriptors and an atomic launch counter.
  */
 #ifndef ORDA_B200_H_
 #define ORDA_B200_H_
@@ -147,6 +147,9 @@ int32_t orda_abi_version(void);
 
 /* sizeof(orda_distill_args_t) as compiled into the library (lets FFI callers check their layout). */
 size_t orda_args_struct_size(void);
+
+/* Number of kernels this library has launched in this process (monotonic; for launch accounting). */
+uint64_t orda_kernel_launches(void);
 
 /* Human-readable text for a status code. */
 const char* orda_status_string(int32_t status);

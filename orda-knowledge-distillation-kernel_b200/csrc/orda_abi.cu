@@ -11,6 +11,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 #include <mutex>
 #include <type_traits>
@@ -24,6 +25,9 @@
 using namespace orda;
 
 namespace {
+
+std::atomic<uint64_t> g_launches{0};
+inline void count_launch(uint64_t n = 1) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -77,7 +81,7 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 size_t esize(int dtype) { return dtype == ORDA_F32 ? 4 : 2; }
 
-constexpr int64_t kDefaultWorkspaceLogitBytes = int64_t(2) << 30;  // bound of the logits chunk buffers
+constexpr int64_t kDefaultWorkspaceLogitBytes = int64_t(4) << 30;  // bound of the logits chunk buffers
 
 struct Plan {
   // problem classification
@@ -190,6 +194,7 @@ int launch_tc(TcGemmParams& prm, int64_t M, int64_t N, cudaStream_t stream, int 
   auto k = tc_gemm_kernel<BN, A_MN, B_MN, MODE, EPI, T16>;
   set_smem(k, S::kSmemBytes);
   const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms()));
+  count_launch();
   k<<<grid, kGemmThreads, S::kSmemBytes, stream>>>(prm);
   return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
 }
@@ -305,6 +310,7 @@ int dw_tc(const orda_distill_args_t* a, const Plan& P, const void* dz0, const vo
 void simt_gemm(const float* A, int64_t sam, int64_t sak, const float* B, int64_t sbn, int64_t sbk, float* out,
                int64_t ldo, int64_t M, int64_t N, int64_t K, int accumulate, cudaStream_t s) {
   dim3 grid(static_cast<unsigned>(cdiv(N, kSimtTile)), static_cast<unsigned>(cdiv(M, kSimtTile)));
+  count_launch();
   simt_gemm_f32_kernel<<<grid, 256, 0, s>>>(A, sam, sak, B, sbn, sbk, out, ldo, M, N, K, accumulate);
 }
 
@@ -325,6 +331,7 @@ int forward_f32(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const 
   f.flags |= F_WRITE_WS_S | (P.teacher_acc ? F_WRITE_WS_T : 0u);  // shift in place
   const int64_t total = c.rows * P.n_vtiles;
   const int grid = static_cast<int>(std::min<int64_t>(cdiv(total, 128), 8192));
+  count_launch();
   if (P.teacher_acc) fwd_stats_gmem_kernel<true><<<grid, 128, 0, s>>>(f);
   else fwd_stats_gmem_kernel<false><<<grid, 128, 0, s>>>(f);
   return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
@@ -337,6 +344,7 @@ int row_phases(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const C
   RowParams r = row_params(a, P, ws, c);
   if (do_merge) {
     const int grid = static_cast<int>(std::min<int64_t>(cdiv(c.rows, 8), 65535));
+    count_launch();
     row_merge_kernel<<<grid, 256, 0, s>>>(r);
   }
   if (!do_loss_and_sweeps) return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
@@ -346,12 +354,15 @@ int row_phases(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const C
   if (P.jsd && !row_sums_ext) {
     float* sums = reinterpret_cast<float*>(ws + P.off_row_sums);
     set_smem(jsd_sweep_kernel<WsT>, static_cast<uint32_t>(sweep_smem));
+    count_launch();
     jsd_sweep_kernel<WsT><<<sweep_grid, 256, sweep_smem, s>>>(r, sums);
   }
   if (row_sums_ext) r.row_sums = row_sums_ext;
+  count_launch();
   row_loss_kernel<<<static_cast<int>(cdiv(c.rows, 256)), 256, 0, s>>>(r);
   if (P.any_grad) {
     set_smem(grad_sweep_kernel<WsT>, static_cast<uint32_t>(sweep_smem));
+    count_launch();
     grad_sweep_kernel<WsT><<<sweep_grid, 256, sweep_smem, s>>>(r);
   }
   return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
@@ -506,6 +517,7 @@ int run_all(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, cudaStream
     if ((rc = grad_gemms<WsT>(a, P, ws, c, r0 == 0, s, &pm, pm.on))) return rc;
   }
   const float* rl = a->out_row_losses ? a->out_row_losses : reinterpret_cast<const float*>(ws + P.off_row_losses);
+  count_launch();
   finalize_kernel<<<1, 1024, 0, s>>>(rl, a->n_rows, a->labels, a->n_rows, a->ignore_index, a->reduction, P.flags,
                                      a->student_ce_weight, a->teacher_ce_weight, a->kl_weight, a->out_reduced);
   return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
@@ -524,6 +536,8 @@ int dispatch_all(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, cudaS
 extern "C" {
 
 int32_t orda_abi_version(void) { return ORDA_ABI_VERSION; }
+
+uint64_t orda_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
 
 size_t orda_args_struct_size(void) { return sizeof(orda_distill_args_t); }
 
@@ -585,6 +599,7 @@ int32_t orda_shard_forward(const orda_distill_args_t* args, void* workspace, siz
 int32_t orda_merge_row_stats(const float* gathered, int32_t world, int64_t n_rows, float* row_stats, void* stream) {
   if (!gathered || !row_stats || world < 1 || n_rows <= 0) return ORDA_ERR_INVALID_ARGUMENT;
   const int grid = static_cast<int>(std::min<int64_t>(cdiv(n_rows, 256), 65535));
+  count_launch();
   merge_records_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(gathered, world, n_rows, row_stats);
   return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
 }
@@ -603,6 +618,7 @@ int32_t orda_shard_jsd_partials(const orda_distill_args_t* args, void* workspace
   r.row_stats = const_cast<float*>(row_stats);
   const size_t smem = sizeof(float) * (2 * P.n_vtiles + 32);
   const int grid = static_cast<int>(std::min<int64_t>(c.rows, 8 * num_sms()));
+  count_launch();
   switch (args->compute_dtype) {
     case ORDA_BF16: set_smem(jsd_sweep_kernel<__nv_bfloat16>, (uint32_t)smem); jsd_sweep_kernel<__nv_bfloat16><<<grid, 256, smem, s>>>(r, row_sums); break;
     case ORDA_F16: set_smem(jsd_sweep_kernel<__half>, (uint32_t)smem); jsd_sweep_kernel<__half><<<grid, 256, smem, s>>>(r, row_sums); break;
@@ -638,6 +654,7 @@ int32_t orda_shard_backward(const orda_distill_args_t* args, void* workspace, si
   }
   if (rc) return rc;
   const float* rl = args->out_row_losses ? args->out_row_losses : reinterpret_cast<const float*>(ws + P.off_row_losses);
+  count_launch();
   finalize_kernel<<<1, 1024, 0, s>>>(rl, args->n_rows, args->labels, args->n_rows, args->ignore_index,
                                      args->reduction, P.flags, args->student_ce_weight, args->teacher_ce_weight,
                                      args->kl_weight, args->out_reduced);

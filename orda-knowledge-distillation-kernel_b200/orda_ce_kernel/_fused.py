@@ -13,7 +13,11 @@ Gradient presence matches the reference per mode:
 """
 from __future__ import annotations
 
+import contextlib
+import threading
 from dataclasses import dataclass
+
+import ctypes
 
 import torch
 from torch.autograd.function import once_differentiable
@@ -29,6 +33,23 @@ _MODE_CODE = {
     "precomputed_logits": _native.TEACHER_LOGITS,
     "precomputed_hidden": _native.TEACHER_HIDDEN,
 }
+
+
+_HOOKS = threading.local()
+
+
+@contextlib.contextmanager
+def instrument(phase_events=None, dweight_done_event=None, dweight_first=False):
+    """Attach CUDA events to the fused calls made inside the block (benchmarks / overlap):
+    ``phase_events`` - 2*PHASES ``torch.cuda.Event(enable_timing=True)`` recorded around each phase;
+    ``dweight_done_event`` - recorded when the weight gradients are complete;
+    ``dweight_first`` - run the dW GEMMs before the dH GEMMs."""
+    prev = getattr(_HOOKS, "value", None)
+    _HOOKS.value = (phase_events, dweight_done_event, dweight_first)
+    try:
+        yield
+    finally:
+        _HOOKS.value = prev
 
 
 @dataclass(frozen=True)
@@ -177,6 +198,17 @@ class FusedDistillFunction(torch.autograd.Function):
         a.grad_teacher_hidden, a.grad_teacher_weight = _ptr(g_ht), _ptr(g_wt)
         a.grad_weight_fp32 = int(f32_acc)
         a.device_status = _ptr(status)
+
+        hooks = getattr(_HOOKS, "value", None)
+        if hooks is not None:
+            ev, done, first = hooks
+            if ev is not None:
+                handles = (ctypes.c_void_p * (2 * _native.PHASES))(*[e.cuda_event for e in ev])
+                ctx._phase_handles = handles  # keep alive for the call
+                a.phase_events = ctypes.cast(handles, ctypes.c_void_p)
+            if done is not None:
+                a.dweight_done_event = done.cuda_event
+            a.dweight_first = int(bool(first))
 
         ws_bytes = int(lib.orda_distill_workspace_bytes(a))
         ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)

@@ -80,6 +80,7 @@ class DistillArgs(ctypes.Structure):
 EXPORTED_SYMBOLS = (
     "orda_abi_version",
     "orda_args_struct_size",
+    "orda_kernel_launches",
     "orda_status_string",
     "orda_distill_workspace_bytes",
     "orda_distill_fwdbwd",
@@ -102,6 +103,8 @@ def _declare(lib):
     lib.orda_abi_version.argtypes = []
     lib.orda_args_struct_size.restype = ctypes.c_size_t
     lib.orda_args_struct_size.argtypes = []
+    lib.orda_kernel_launches.restype = ctypes.c_uint64
+    lib.orda_kernel_launches.argtypes = []
     lib.orda_status_string.restype = ctypes.c_char_p
     lib.orda_status_string.argtypes = [_i32]
     lib.orda_distill_workspace_bytes.restype = ctypes.c_size_t
