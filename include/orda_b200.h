@@ -169,6 +169,21 @@ size_t orda_distill_workspace_bytes(const orda_distill_args_t* args);
 int32_t orda_distill_fwdbwd(const orda_distill_args_t* args, void* workspace, size_t workspace_bytes,
                             void* stream);
 
+/* Size of the library-owned scratch used by orda_distill_fwdbwd_static_ws (32 MiB per GPU). */
+#define ORDA_STATIC_WORKSPACE_BYTES (32u << 20)
+
+/* No counterpart in the reference. Same computation and outputs as orda_distill_fwdbwd, for callers
+ * that cannot allocate device memory themselves (for example a host runtime that hands out only
+ * pre-registered input/output buffers, or code running where a cudaMalloc would synchronise or is
+ * forbidden). The scratch lives in a fixed 32 MiB array inside the library, which every GPU that loads
+ * the library keeps until the process exits; the call allocates nothing. Rows are processed in
+ * chunks small enough to fit; if even one 128-row chunk (or the per-row loss buffer, 3 x n_rows
+ * floats) does not fit, it returns ORDA_ERR_WORKSPACE and launches nothing. The first call on each
+ * device looks up the array's device address (make it before any stream capture). All calls share
+ * the one array: calls that overlap on the GPU (other streams, other host threads) race and must be
+ * serialised by the caller. */
+int32_t orda_distill_fwdbwd_static_ws(const orda_distill_args_t* args, void* stream);
+
 /* ---- vocab-sharded multi-GPU building blocks (one call per rank; NCCL stays with the caller) ----
  * Per-row statistics record exchanged between ranks: ORDA_ROW_STATS floats per row. */
 #define ORDA_ROW_STATS 16

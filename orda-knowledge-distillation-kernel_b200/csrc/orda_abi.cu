@@ -689,3 +689,50 @@ int32_t orda_debug_gemm(int32_t dtype, int32_t a_mn, int32_t b_mn, const void* A
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- allocation-free variant
+// Library-owned scratch for callers that cannot allocate device memory. Host code must not pass
+// the symbol itself to a kernel (on the host it is only a stand-in); the device address is looked
+// up once per device with cudaGetSymbolAddress while that device is current.
+static __device__ __align__(256) uint8_t g_orda_static_ws[ORDA_STATIC_WORKSPACE_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_static_ws_mutex;
+void* g_static_ws_ptr[kMaxDevices] = {};
+
+int static_ws_address(void** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return ORDA_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lock(g_static_ws_mutex);
+  if (!g_static_ws_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_orda_static_ws) != cudaSuccess || !p) return ORDA_ERR_CUDA;
+    g_static_ws_ptr[dev] = p;
+  }
+  *out = g_static_ws_ptr[dev];
+  return ORDA_OK;
+}
+}  // namespace
+
+extern "C" int32_t orda_distill_fwdbwd_static_ws(const orda_distill_args_t* args, void* stream) {
+  int rc = check_args(args);
+  if (rc) return rc;
+  // largest chunk (a multiple of 128 rows, or all rows) whose workspace fits in the static array
+  int64_t C = args->chunk_rows > 0 ? std::min<int64_t>(args->chunk_rows, args->n_rows) : args->n_rows;
+  Plan P = make_plan(args, C);
+  while (P.total > ORDA_STATIC_WORKSPACE_BYTES && C > kTileRows) {
+    C = std::max<int64_t>(kTileRows, (C / 2) / kTileRows * kTileRows);
+    P = make_plan(args, C);
+  }
+  if (P.total > ORDA_STATIC_WORKSPACE_BYTES) return ORDA_ERR_WORKSPACE;
+  if ((rc = check_operands(args, P))) return rc;
+  void* ws = nullptr;
+  if ((rc = static_ws_address(&ws))) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // the array keeps the previous call's contents; the label-logit slots are cleared so no row can
+  // read a value left behind by an earlier call
+  if (cudaMemsetAsync(static_cast<uint8_t*>(ws) + P.off_label, 0, P.off_row_stats - P.off_label, s) != cudaSuccess)
+    return ORDA_ERR_CUDA;
+  return dispatch_all(args, P, static_cast<uint8_t*>(ws), s);
+}

@@ -37,6 +37,7 @@ OUT_LOSS, OUT_STUDENT_CE, OUT_TEACHER_CE, OUT_KL, OUT_MEAN_SCALE = 0, 1, 2, 3, 4
 OUT_SUM_STUDENT_CE, OUT_SUM_TEACHER_CE, OUT_SUM_KL, OUT_COUNT = 5, 6, 7, 8
 OUT_SLOTS = 9
 ROW_STATS = 16
+STATIC_WORKSPACE_BYTES = 32 << 20
 PHASE_LOGITS, PHASE_ROWS, PHASE_DHIDDEN, PHASE_DWEIGHT = 0, 1, 2, 3
 PHASES = 4
 
@@ -84,6 +85,7 @@ EXPORTED_SYMBOLS = (
     "orda_status_string",
     "orda_distill_workspace_bytes",
     "orda_distill_fwdbwd",
+    "orda_distill_fwdbwd_static_ws",
     "orda_shard_workspace_bytes",
     "orda_shard_forward",
     "orda_merge_row_stats",
@@ -111,6 +113,8 @@ def _declare(lib):
     lib.orda_distill_workspace_bytes.argtypes = [P]
     lib.orda_distill_fwdbwd.restype = _i32
     lib.orda_distill_fwdbwd.argtypes = [P, _vp, ctypes.c_size_t, _vp]
+    lib.orda_distill_fwdbwd_static_ws.restype = _i32
+    lib.orda_distill_fwdbwd_static_ws.argtypes = [P, _vp]
     lib.orda_shard_workspace_bytes.restype = ctypes.c_size_t
     lib.orda_shard_workspace_bytes.argtypes = [P]
     lib.orda_shard_forward.restype = _i32
