@@ -19,6 +19,11 @@ int32_t orda_debug_gemm(int32_t dtype, int32_t a_mn, int32_t b_mn, const void* A
                         int64_t ldb, int64_t M, int64_t N, int64_t K, float* out, int64_t ldo, int32_t* status,
                         void* stream);
 
+/* Same contract, computed by the CTA-pair (cta_group::2) kernel with 256 x 256 tiles. */
+int32_t orda_debug_gemm_pair(int32_t dtype, int32_t a_mn, int32_t b_mn, const void* A, int64_t lda, const void* B,
+                             int64_t ldb, int64_t M, int64_t N, int64_t K, float* out, int64_t ldo, int32_t* status,
+                             void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -11,26 +11,21 @@ namespace orda {
 
 constexpr int kTileRows = 128;   // rows of one GEMM tile (TMEM lanes)
 constexpr int kVocabTile = 128;  // vocab columns covered by one statistics record
-constexpr int kTileStats = 8;    // floats per (row, vocab tile) record
+constexpr int kTileStats = 2;    // floats per (row, vocab tile) record
 constexpr int kRowStats = 16;    // floats per merged row record (== ORDA_ROW_STATS)
 
-// Tile record fields (one per row and 128-column vocab tile):
+// Tile record fields (one per row and 128-column vocab tile): the maxima the workspace logits are
+// shifted by.
 enum TileStat {
-  TS_MAX_S = 0,   // max_j z_j                      (student logits of the tile)
-  TS_SUM1_S = 1,  // sum exp(z_j - max)             (softmax at T = 1, cross entropy)
-  TS_SUMT_S = 2,  // sum exp((z_j - max) / T)       (softmax at T, distillation)
-  TS_MAX_T = 3,   // same three for the teacher logits u_j
-  TS_SUM1_T = 4,
-  TS_SUMT_T = 5,
-  TS_CROSS = 6,   // forward: sum exp((u-max_t)/T) (u-z)/T ; reverse: sum exp((z-max_s)/T) (z-u)/T
-  TS_UNUSED = 7,
+  TS_MAX_S = 0,   // max_j z_j of the tile (student)
+  TS_MAX_T = 1,   // max_j u_j of the tile (teacher)
 };
 
 // Merged row record fields (the unit exchanged between vocab shards):
 enum RowStat {
   RS_MAX_S = 0, RS_SUM1_S = 1, RS_SUMT_S = 2,
   RS_MAX_T = 3, RS_SUM1_T = 4, RS_SUMT_T = 5,
-  RS_CROSS = 6,        // TS_CROSS merged to the row maxima
+  RS_CROSS = 6,        // divergence cross term, relative to the row maxima
   RS_LABEL_S = 7,      // student logit at the label (valid when RS_HAS_LABEL == 1)
   RS_LABEL_T = 8,      // teacher logit at the label
   RS_HAS_LABEL = 9,    // 1 if this shard (or the merge) holds the label column

@@ -3,15 +3,13 @@
 // One thread owns one logits row of a 128-row x 128-column tile (student accumulator, and the
 // teacher accumulator or the caller's teacher logits). It computes, without ever writing the
 // un-shifted logits to memory:
-//   - the tile maxima and the online-softmax sums at T = 1 and at T (student and teacher),
-//   - the forward-KL (or reverse-KL) cross term needed to evaluate the divergence from merged
-//     row statistics,
+//   - the tile maxima (student and teacher),
 //   - the label logit (exact fp32 accumulator value),
 // and stores the logits shifted by the tile maximum into the bounded chunk workspace in the
 // compute dtype (values near the row maximum, which dominate softmax, keep full relative precision).
 //
-// This is the statistics half of the reference row kernels (ops/tied_teacher.py:54-141,
-// ops/separate_teacher.py, ops/precomputed_teacher.py:53-101), moved into the GEMM epilogue.
+// Together with row_stats_kernel this is the statistics half of the reference row kernels
+// (ops/tied_teacher.py:54-141, ops/separate_teacher.py, ops/precomputed_teacher.py:53-101).
 #pragma once
 
 #include "distill_common.cuh"
@@ -39,23 +37,6 @@ struct FwdEpiParams {
   float* label_logits;            // [rows][2]
 };
 
-__device__ __forceinline__ void load_teacher_gmem(const FwdEpiParams& p, int64_t row, int64_t col0, int count,
-                                                  float (&v)[32]) {
-  if (p.tg_dtype == ORDA_F32) {
-    const float* q = static_cast<const float*>(p.t_gmem) + row * p.ld_tg + col0;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = j < count ? __ldg(q + j) : 0.f;
-  } else if (p.tg_dtype == ORDA_BF16) {
-    const __nv_bfloat16* q = static_cast<const __nv_bfloat16*>(p.t_gmem) + row * p.ld_tg + col0;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = j < count ? __bfloat162float(q[j]) : 0.f;
-  } else {
-    const __half* q = static_cast<const __half*>(p.t_gmem) + row * p.ld_tg + col0;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = j < count ? __half2float(q[j]) : 0.f;
-  }
-}
-
 template <typename WsT>
 __device__ __forceinline__ void store_chunk32(WsT* dst, const float (&v)[32]) {
   if constexpr (sizeof(WsT) == 2) {
@@ -79,18 +60,18 @@ __device__ __forceinline__ void store_chunk32(WsT* dst, const float (&v)[32]) {
 // `src.load(acc, chunk, v)` yields 32 fp32 logits of accumulator `acc` (0 student, 1 teacher) for
 // columns [32*chunk, 32*chunk+32) of the tile. For TMEM sources the call is warp-collective, so
 // every lane calls it the same number of times whatever its row.
+//
+// Per (row, 128-column vocab tile) the epilogue produces only what needs the fp32 accumulator:
+// the tile maximum of each distribution, the logits shifted by that maximum in the compute dtype,
+// and the exact label logit. The exponentials (softmax sums, divergence cross terms) are computed
+// by the memory-bound row pass that streams the workspace anyway, which keeps the transcendental
+// pipe out of the GEMM's critical path.
 template <typename WsT, bool kTeacherAcc, class Src>
 __device__ __forceinline__ void fwd_tile_stats(const FwdEpiParams& p, int64_t row, bool row_ok, int64_t n0,
                                                int tile, Src& src) {
   constexpr int kChunks = kVocabTile / 32;
   const uint32_t f = p.flags;
-  const bool teacher = (f & F_TEACHER) != 0;
-  const bool t_gmem = (f & F_TEACHER_GMEM) != 0;
-  const bool t_not_one = (f & F_T_NOT_ONE) != 0;
-  const bool need_t1 = (f & F_TEACHER_CE) != 0;
-  const bool kl = (f & F_KL) != 0;
-  const bool kl_rev = (f & F_KL_REVERSE) != 0;
-  const float inv_t = p.inv_t;
+  const bool teacher = kTeacherAcc && (f & F_TEACHER) != 0;
   const int nvalid = static_cast<int>((p.vocab - n0 < (int64_t)kVocabTile ? p.vocab - n0 : (int64_t)kVocabTile));
 
   int label_col = -1;
@@ -113,73 +94,39 @@ __device__ __forceinline__ void fwd_tile_stats(const FwdEpiParams& p, int64_t ro
     for (int j = 0; j < 32; ++j)
       if (c * 32 + j < nvalid) ms = fmaxf(ms, v[j]);
     if (teacher) {
-      if constexpr (kTeacherAcc) {
-        src.load(1, c, v);
-      } else {
-        if (row_ok) load_teacher_gmem(p, row, n0 + c * 32, min(32, nvalid - c * 32), v);
-      }
+      src.load(1, c, v);
 #pragma unroll
       for (int j = 0; j < 32; ++j)
         if (c * 32 + j < nvalid) mt = fmaxf(mt, v[j]);
     }
   }
-  (void)t_gmem;
 
-  // ---- pass 2: sums, cross term, label logit, shifted logits
-  float s1s = 0.f, sts = 0.f, s1t = 0.f, stt = 0.f, cross = 0.f, zy_s = 0.f, zy_t = 0.f;
+  // ---- pass 2: shifted logits and the label logit
+  float zy_s = 0.f, zy_t = 0.f;
   const int64_t ws_row = row * p.ld_ws + n0;
 #pragma unroll 1
   for (int c = 0; c < kChunks; ++c) {
-    float vs[32], vt[32];
-    src.load(0, c, vs);
-    if (teacher) {
-      if constexpr (kTeacherAcc) {
-        src.load(1, c, vt);
-      } else {
-        if (row_ok) load_teacher_gmem(p, row, n0 + c * 32, min(32, nvalid - c * 32), vt);
-      }
-    }
+    float v[32];
+    src.load(0, c, v);
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-      const bool valid = (c * 32 + j) < nvalid;
-      const float z = vs[j];
-      const float d = z - ms;
-      const float e1 = valid ? fast_exp(d) : 0.f;
-      const float et_s = t_not_one ? (valid ? fast_exp(d * inv_t) : 0.f) : e1;
-      s1s += e1;
-      sts += et_s;
-      if (c * 32 + j == label_col) zy_s = z;
-      vs[j] = d;
-      if (teacher) {
-        const float u = vt[j];
-        const float dt = u - mt;
-        float e1t = 0.f, ett = 0.f;
-        if (valid) {
-          if (!t_not_one) {
-            e1t = fast_exp(dt);
-            ett = e1t;
-          } else {
-            if (need_t1) e1t = fast_exp(dt);
-            if (kl) ett = fast_exp(dt * inv_t);
-          }
-        }
-        s1t += e1t;
-        stt += ett;
-        if (kl && valid) cross += kl_rev ? et_s * (z - u) * inv_t : ett * (u - z) * inv_t;
-        if (c * 32 + j == label_col) zy_t = u;
-        vt[j] = dt;
-      }
+      if (c * 32 + j == label_col) zy_s = v[j];
+      v[j] -= ms;
     }
-    if (row_ok) {
-      if (f & F_WRITE_WS_S) store_chunk32<WsT>(static_cast<WsT*>(p.ws_s) + ws_row + c * 32, vs);
-      if (teacher && (f & F_WRITE_WS_T)) store_chunk32<WsT>(static_cast<WsT*>(p.ws_t) + ws_row + c * 32, vt);
+    if (row_ok && (f & F_WRITE_WS_S)) store_chunk32<WsT>(static_cast<WsT*>(p.ws_s) + ws_row + c * 32, v);
+    if (teacher) {
+      src.load(1, c, v);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (c * 32 + j == label_col) zy_t = v[j];
+        v[j] -= mt;
+      }
+      if (row_ok && (f & F_WRITE_WS_T)) store_chunk32<WsT>(static_cast<WsT*>(p.ws_t) + ws_row + c * 32, v);
     }
   }
 
   if (row_ok) {
-    float4* rec = reinterpret_cast<float4*>(p.tile_stats + (row * p.n_vtiles + tile) * kTileStats);
-    rec[0] = make_float4(ms, s1s, sts, mt);
-    rec[1] = make_float4(s1t, stt, cross, 0.f);
+    reinterpret_cast<float2*>(p.tile_stats)[row * p.n_vtiles + tile] = make_float2(ms, mt);
     if (label_col >= 0) {
       p.label_logits[row * 2 + 0] = zy_s;
       p.label_logits[row * 2 + 1] = zy_t;

@@ -67,15 +67,29 @@ struct GemmShape {
   static_assert(kStages >= 2, "need at least two pipeline stages");
 };
 
-__device__ __forceinline__ void tile_coords(int32_t t, int32_t m_tiles, int32_t n_tiles, int32_t group_m,
+// Grouped rasterisation of the persistent tile index. group > 0: groups of `group` m-tiles, m fastest
+// inside a group (consecutive tiles share the B tile). group < 0: groups of -group n-tiles, n fastest
+// (consecutive tiles share the A tile).
+__device__ __forceinline__ void tile_coords(int32_t t, int32_t m_tiles, int32_t n_tiles, int32_t group,
                                             int32_t& mt, int32_t& nt) {
-  const int32_t per_group = group_m * n_tiles;
-  const int32_t g = t / per_group;
-  const int32_t first_m = g * group_m;
-  const int32_t gm = min(group_m, m_tiles - first_m);
-  const int32_t local = t - g * per_group;
-  mt = first_m + local % gm;
-  nt = local / gm;
+  if (group > 0) {
+    const int32_t per_group = group * n_tiles;
+    const int32_t g = t / per_group;
+    const int32_t first_m = g * group;
+    const int32_t gm = min(group, m_tiles - first_m);
+    const int32_t local = t - g * per_group;
+    mt = first_m + local % gm;
+    nt = local / gm;
+  } else {
+    const int32_t gsz = -group;
+    const int32_t per_group = gsz * m_tiles;
+    const int32_t g = t / per_group;
+    const int32_t first_n = g * gsz;
+    const int32_t gn = min(gsz, n_tiles - first_n);
+    const int32_t local = t - g * per_group;
+    nt = first_n + local % gn;
+    mt = local / gn;
+  }
 }
 
 template <bool MN>

@@ -12,11 +12,13 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <type_traits>
 
 #include "gemm_tc.cuh"
+#include "gemm_tc2.cuh"
 #include "orda_b200.h"
 #include "orda_b200_testing.h"
 #include "row_kernels.cuh"
@@ -77,6 +79,11 @@ int num_sms() {
   return n > 0 ? n : 148;
 }
 
+int env_group(const char* name, int dflt) {  // tuning knob for tile rasterisation
+  const char* v = getenv(name);
+  return v ? atoi(v) : dflt;
+}
+
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 size_t esize(int dtype) { return dtype == ORDA_F32 ? 4 : 2; }
@@ -134,8 +141,9 @@ Plan make_plan(const orda_distill_args_t* a, int64_t chunk_override) {
   p.grad_t = p.teacher_ce && ((tied && (a->need_grad_teacher_hidden || a->need_grad_weight)) ||
                               (sep && (a->need_grad_teacher_hidden || a->need_grad_teacher_weight)));
   p.any_grad = p.grad_s || p.grad_t;
-  p.write_ws_s = p.grad_s || p.jsd || p.grad_t;  // grad sweep / JSD sweep read the student row
-  p.write_ws_t = p.teacher_acc && (p.grad_t || (p.kl && (p.grad_s || p.jsd)));
+  // the row statistics pass streams the shifted logits, so they are always kept
+  p.write_ws_s = true;
+  p.write_ws_t = p.teacher_acc;
   uint32_t f = 0;
   if (p.teacher) f |= F_TEACHER;
   if (p.teacher_gmem) f |= F_TEACHER_GMEM;
@@ -199,6 +207,23 @@ int launch_tc(TcGemmParams& prm, int64_t M, int64_t N, cudaStream_t stream, int 
   return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
 }
 
+template <bool A_MN, bool B_MN, int AMODE, bool TWO_SEG, int EPI, typename T16>
+int launch_tc2(TcGemmParams& prm, int64_t M_tiles, int64_t N, cudaStream_t stream, int group_m) {
+  using S = PairShape<AMODE>;
+  prm.m_tiles = static_cast<int32_t>(M_tiles);
+  prm.n_tiles = static_cast<int32_t>(cdiv(N, kPairBN));
+  prm.group_m = group_m;
+  const int64_t tiles = (int64_t)prm.m_tiles * prm.n_tiles;
+  if (tiles <= 0) return ORDA_OK;
+  if (tiles > INT32_MAX) return ORDA_ERR_UNSUPPORTED;
+  auto k = tc2_gemm_kernel<A_MN, B_MN, AMODE, TWO_SEG, EPI, T16>;
+  set_smem(k, S::kSmemBytes);
+  const int pairs = static_cast<int>(std::min<int64_t>(tiles, num_sms() / 2));
+  count_launch();
+  k<<<2 * pairs, kGemmThreads, S::kSmemBytes, stream>>>(prm);
+  return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
+}
+
 struct ChunkPtrs {
   const uint8_t* hs; const uint8_t* ht; const int64_t* labels;
   int64_t r0, rows;
@@ -258,8 +283,10 @@ int forward_tc(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const C
   if ((rc = make_operand_map(&prm.b0, dt, a->weight, false, a->vocab, a->hidden, a->ld_weight, kVocabTile))) return rc;
   prm.kb0 = static_cast<int32_t>(cdiv(a->hidden, kBK));
   if (P.teacher_acc && a->teacher_mode == ORDA_TEACHER_TIED) {
-    if ((rc = make_operand_map(&prm.a1, dt, c.ht, false, c.rows, a->hidden, a->ld_teacher_hidden, kTileRows))) return rc;
-    return launch_tc<kVocabTile, false, false, GM_SHARED_B, EPI_FWD_STATS, T16>(prm, c.rows, a->vocab, s, 16);
+    // CTA-pair kernel: 64 student rows + the same 64 teacher rows per CTA, half the lm_head tile per CTA
+    if ((rc = make_operand_map(&prm.a0, dt, c.hs, false, c.rows, a->hidden, a->ld_student_hidden, 64))) return rc;
+    if ((rc = make_operand_map(&prm.a1, dt, c.ht, false, c.rows, a->hidden, a->ld_teacher_hidden, 64))) return rc;
+    return launch_tc2<false, false, A_INTERLEAVE, false, EPI_FWD_STATS, T16>(prm, cdiv(c.rows, 128), a->vocab, s, env_group("ORDA_GROUP_FWD", 16));
   }
   if (P.teacher_acc) {
     if ((rc = make_operand_map(&prm.a1, dt, c.ht, false, c.rows, a->teacher_hidden, a->ld_teacher_hidden, kTileRows))) return rc;
@@ -267,7 +294,7 @@ int forward_tc(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const C
     prm.kb1 = static_cast<int32_t>(cdiv(a->teacher_hidden, kBK));
     return launch_tc<kVocabTile, false, false, GM_TWO_ACC, EPI_FWD_STATS, T16>(prm, c.rows, a->vocab, s, 16);
   }
-  return launch_tc<kVocabTile, false, false, GM_SINGLE, EPI_FWD_STATS, T16>(prm, c.rows, a->vocab, s, 16);
+  return launch_tc2<false, false, A_PLAIN, false, EPI_FWD_STATS, T16>(prm, cdiv(c.rows, 256), a->vocab, s, 8);
 }
 
 // dH[rows, N] = dZ[rows, V] * Wm[V, N]
@@ -278,10 +305,10 @@ int dh_tc(const orda_distill_args_t* a, const Plan& P, const void* dz, const voi
   prm.status = status;
   int rc;
   if ((rc = make_operand_map(&prm.a0, a->compute_dtype, dz, false, rows, a->vocab, P.vpad, kTileRows))) return rc;
-  if ((rc = make_operand_map(&prm.b0, a->compute_dtype, wmat, true, n, a->vocab, ldw, 256))) return rc;
+  if ((rc = make_operand_map(&prm.b0, a->compute_dtype, wmat, true, n, a->vocab, ldw, 128))) return rc;
   prm.kb0 = static_cast<int32_t>(cdiv(a->vocab, kBK));
   prm.st = StoreEpiParams{out, n, rows, n, 0, 0};
-  return launch_tc<256, false, true, GM_SINGLE, EPI_STORE, T16>(prm, rows, n, s, 8);
+  return launch_tc2<false, true, A_PLAIN, false, EPI_STORE, T16>(prm, cdiv(rows, 256), n, s, env_group("ORDA_GROUP_DH", 8));
 }
 
 // dW[V, N] (+)= dZ0^T H0 (+ dZ1^T H1)
@@ -294,16 +321,16 @@ int dw_tc(const orda_distill_args_t* a, const Plan& P, const void* dz0, const vo
   const int dt = a->compute_dtype;
   int rc;
   if ((rc = make_operand_map(&prm.a0, dt, dz0, true, a->vocab, rows, P.vpad, kTileRows))) return rc;
-  if ((rc = make_operand_map(&prm.b0, dt, h0, true, n, rows, ldh0, 256))) return rc;
+  if ((rc = make_operand_map(&prm.b0, dt, h0, true, n, rows, ldh0, 128))) return rc;
   prm.kb0 = static_cast<int32_t>(cdiv(rows, kBK));
   prm.st = StoreEpiParams{out, n, a->vocab, n, out_f32, accumulate};
   if (dz1) {
     if ((rc = make_operand_map(&prm.a1, dt, dz1, true, a->vocab, rows, P.vpad, kTileRows))) return rc;
-    if ((rc = make_operand_map(&prm.b1, dt, h1, true, n, rows, ldh1, 256))) return rc;
+    if ((rc = make_operand_map(&prm.b1, dt, h1, true, n, rows, ldh1, 128))) return rc;
     prm.kb1 = prm.kb0;
-    return launch_tc<256, true, true, GM_TWO_SEG, EPI_STORE, T16>(prm, a->vocab, n, s, 8);
+    return launch_tc2<true, true, A_PLAIN, true, EPI_STORE, T16>(prm, cdiv(a->vocab, 256), n, s, env_group("ORDA_GROUP_DW", 8));
   }
-  return launch_tc<256, true, true, GM_SINGLE, EPI_STORE, T16>(prm, a->vocab, n, s, 8);
+  return launch_tc2<true, true, A_PLAIN, false, EPI_STORE, T16>(prm, cdiv(a->vocab, 256), n, s, env_group("ORDA_GROUP_DW", 8));
 }
 
 // ------------------------------------------------------------------ fp32 (SIMT) phases
@@ -342,28 +369,25 @@ template <typename WsT>
 int row_phases(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const ChunkPtrs& c, cudaStream_t s,
                bool do_merge, bool do_loss_and_sweeps, const float* row_stats_ext, const float* row_sums_ext) {
   RowParams r = row_params(a, P, ws, c);
+  // one warp per row, 8 rows per block
+  const int sweep_grid = static_cast<int>(std::min<int64_t>(cdiv(c.rows, 8), 16 * num_sms()));
   if (do_merge) {
-    const int grid = static_cast<int>(std::min<int64_t>(cdiv(c.rows, 8), 65535));
     count_launch();
-    row_merge_kernel<<<grid, 256, 0, s>>>(r);
+    launch_row_stats<WsT>(r, sweep_grid, s);
   }
   if (!do_loss_and_sweeps) return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
   if (row_stats_ext) r.row_stats = const_cast<float*>(row_stats_ext);
-  const size_t sweep_smem = sizeof(float) * (2 * P.n_vtiles + 32);
-  const int sweep_grid = static_cast<int>(std::min<int64_t>(c.rows, 8 * num_sms()));
   if (P.jsd && !row_sums_ext) {
     float* sums = reinterpret_cast<float*>(ws + P.off_row_sums);
-    set_smem(jsd_sweep_kernel<WsT>, static_cast<uint32_t>(sweep_smem));
     count_launch();
-    jsd_sweep_kernel<WsT><<<sweep_grid, 256, sweep_smem, s>>>(r, sums);
+    jsd_sweep_kernel<WsT><<<sweep_grid, 256, 0, s>>>(r, sums);
   }
   if (row_sums_ext) r.row_sums = row_sums_ext;
   count_launch();
   row_loss_kernel<<<static_cast<int>(cdiv(c.rows, 256)), 256, 0, s>>>(r);
   if (P.any_grad) {
-    set_smem(grad_sweep_kernel<WsT>, static_cast<uint32_t>(sweep_smem));
     count_launch();
-    grad_sweep_kernel<WsT><<<sweep_grid, 256, sweep_smem, s>>>(r);
+    launch_grad_sweep<WsT>(r, sweep_grid, s);
   }
   return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
 }
@@ -616,13 +640,12 @@ int32_t orda_shard_jsd_partials(const orda_distill_args_t* args, void* workspace
   const ChunkPtrs c = chunk_ptrs(args, 0, args->n_rows);
   RowParams r = row_params(args, P, ws, c);
   r.row_stats = const_cast<float*>(row_stats);
-  const size_t smem = sizeof(float) * (2 * P.n_vtiles + 32);
-  const int grid = static_cast<int>(std::min<int64_t>(c.rows, 8 * num_sms()));
+  const int grid = static_cast<int>(std::min<int64_t>(cdiv(c.rows, 8), 16 * num_sms()));
   count_launch();
   switch (args->compute_dtype) {
-    case ORDA_BF16: set_smem(jsd_sweep_kernel<__nv_bfloat16>, (uint32_t)smem); jsd_sweep_kernel<__nv_bfloat16><<<grid, 256, smem, s>>>(r, row_sums); break;
-    case ORDA_F16: set_smem(jsd_sweep_kernel<__half>, (uint32_t)smem); jsd_sweep_kernel<__half><<<grid, 256, smem, s>>>(r, row_sums); break;
-    default: set_smem(jsd_sweep_kernel<float>, (uint32_t)smem); jsd_sweep_kernel<float><<<grid, 256, smem, s>>>(r, row_sums); break;
+    case ORDA_BF16: jsd_sweep_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(r, row_sums); break;
+    case ORDA_F16: jsd_sweep_kernel<__half><<<grid, 256, 0, s>>>(r, row_sums); break;
+    default: jsd_sweep_kernel<float><<<grid, 256, 0, s>>>(r, row_sums); break;
   }
   return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
 }
@@ -686,6 +709,33 @@ int32_t orda_debug_gemm(int32_t dtype, int32_t a_mn, int32_t b_mn, const void* A
   if (b_mn) ORDA_DBG(__half, false, true);
   ORDA_DBG(__half, false, false);
 #undef ORDA_DBG
+}
+
+int32_t orda_debug_gemm_pair(int32_t dtype, int32_t a_mn, int32_t b_mn, const void* A, int64_t lda, const void* B,
+                             int64_t ldb, int64_t M, int64_t N, int64_t K, float* out, int64_t ldo, int32_t* status,
+                             void* stream) {
+  if (dtype != ORDA_BF16 && dtype != ORDA_F16) return ORDA_ERR_INVALID_ARGUMENT;
+  TcGemmParams prm{};
+  prm.status = status;
+  int rc;
+  if ((rc = make_operand_map(&prm.a0, dtype, A, a_mn != 0, M, K, lda, kTileRows))) return rc;
+  if ((rc = make_operand_map(&prm.b0, dtype, B, b_mn != 0, N, K, ldb, 128))) return rc;
+  prm.kb0 = static_cast<int32_t>(cdiv(K, kBK));
+  prm.st = StoreEpiParams{out, ldo, M, N, 1, 0};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t mt = cdiv(M, 256);
+#define ORDA_DBG2(T, AM, BM) return launch_tc2<AM, BM, A_PLAIN, false, EPI_STORE, T>(prm, mt, N, s, 8)
+  if (dtype == ORDA_BF16) {
+    if (a_mn && b_mn) ORDA_DBG2(__nv_bfloat16, true, true);
+    if (a_mn) ORDA_DBG2(__nv_bfloat16, true, false);
+    if (b_mn) ORDA_DBG2(__nv_bfloat16, false, true);
+    ORDA_DBG2(__nv_bfloat16, false, false);
+  }
+  if (a_mn && b_mn) ORDA_DBG2(__half, true, true);
+  if (a_mn) ORDA_DBG2(__half, true, false);
+  if (b_mn) ORDA_DBG2(__half, false, true);
+  ORDA_DBG2(__half, false, false);
+#undef ORDA_DBG2
 }
 
 }  // extern "C"

@@ -49,54 +49,6 @@ __device__ __forceinline__ Partial warp_merge(Partial a, double inv_t, bool cros
   return a;
 }
 
-// One warp per row.
-__global__ void row_merge_kernel(RowParams p) {
-  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
-  const int lane = threadIdx.x & 31;
-  const bool teacher = p.flags & F_TEACHER;
-  const bool rev = p.flags & F_KL_REVERSE;
-  const double inv_t = p.inv_t;
-  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; row < p.rows; row += warps) {
-    Partial s{-CUDART_INF, 0.0, 0.0, 0.0}, t{-CUDART_INF, 0.0, 0.0, 0.0};
-    const float* rec = p.tile_stats + row * p.n_vtiles * kTileStats;
-    for (int tile = lane; tile < p.n_vtiles; tile += 32) {
-      const float4 a = reinterpret_cast<const float4*>(rec + tile * kTileStats)[0];
-      const float4 b = reinterpret_cast<const float4*>(rec + tile * kTileStats)[1];
-      Partial ps{a.x, a.y, a.z, rev ? (double)b.z : 0.0};
-      merge_partial(s, ps, inv_t, rev);
-      if (teacher) {
-        Partial pt{a.w, b.x, b.y, rev ? 0.0 : (double)b.z};
-        merge_partial(t, pt, inv_t, !rev);
-      }
-    }
-    s = warp_merge(s, inv_t, rev);
-    if (teacher) t = warp_merge(t, inv_t, !rev);
-    if (lane == 0) {
-      float* out = p.row_stats + row * kRowStats;
-      bool ignored;
-      const int64_t ys = safe_label(p.labels[row], p.ignore_index, p.vocab_total, &ignored);
-      const bool has = !ignored && ys >= p.vocab_offset && ys < p.vocab_offset + p.vocab;
-      if (p.flags & F_VALIDATE) {  // validate labels (debug profile): flag, never trap
-        const int64_t y = p.labels[row];
-        if (y != p.ignore_index && (y < 0 || y >= p.vocab_total)) atomicCAS(p.status, 0, ORDA_ERR_LABEL_RANGE);
-      }
-      out[RS_MAX_S] = (float)s.max_v;
-      out[RS_SUM1_S] = (float)s.sum1;
-      out[RS_SUMT_S] = (float)s.sumt;
-      out[RS_MAX_T] = (float)t.max_v;
-      out[RS_SUM1_T] = (float)t.sum1;
-      out[RS_SUMT_T] = (float)t.sumt;
-      out[RS_CROSS] = (float)(rev ? s.cross : t.cross);
-      out[RS_LABEL_S] = has ? p.label_logits[row * 2] : 0.f;
-      out[RS_LABEL_T] = has ? p.label_logits[row * 2 + 1] : 0.f;
-      out[RS_HAS_LABEL] = has ? 1.f : 0.f;
-      out[10] = rev ? 0.f : 1.f;  // cross term follows the teacher maxima
-      out[11] = p.inv_t;
-      for (int k = 12; k < kRowStats; ++k) out[k] = 0.f;
-    }
-  }
-}
-
 // gathered[world][rows][kRowStats] -> out[rows][kRowStats]
 __global__ void merge_records_kernel(const float* gathered, int world, int64_t rows, float* out) {
   for (int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; row < rows; row += (int64_t)gridDim.x * blockDim.x) {
@@ -127,36 +79,40 @@ __global__ void merge_records_kernel(const float* gathered, int world, int64_t r
   }
 }
 
-// One thread per row: per-row losses from the (global) row record.
-__global__ void row_loss_kernel(RowParams p) {
-  for (int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; row < p.rows; row += (int64_t)gridDim.x * blockDim.x) {
-    const float* r = p.row_stats + row * kRowStats;
-    bool ignored;
-    safe_label(p.labels[row], p.ignore_index, p.vocab_total, &ignored);
-    double ce_s = 0.0, ce_t = 0.0, div = 0.0;
-    if (!ignored) {
-      const double lse_s = (double)r[RS_MAX_S] + log((double)r[RS_SUM1_S]);
-      ce_s = lse_s - (double)r[RS_LABEL_S];
-      if (p.flags & F_TEACHER_CE) {
-        const double lse_t = (double)r[RS_MAX_T] + log((double)r[RS_SUM1_T]);
-        ce_t = lse_t - (double)r[RS_LABEL_T];
-      }
-      if (p.flags & F_KL) {
-        const double t = p.temperature, it = p.inv_t;
-        if (p.flags & F_JSD) {
-          div = p.row_sums[row * 2] * t * t;
-        } else {
-          const double lse_st = (double)r[RS_MAX_S] * it + log((double)r[RS_SUMT_S]);
-          const double lse_tt = (double)r[RS_MAX_T] * it + log((double)r[RS_SUMT_T]);
-          if (p.flags & F_KL_REVERSE) div = ((double)r[RS_CROSS] / r[RS_SUMT_S] - lse_st + lse_tt) * t * t;
-          else div = ((double)r[RS_CROSS] / r[RS_SUMT_T] - lse_tt + lse_st) * t * t;
-        }
+// Per-row losses from the (global) row record.
+__device__ __forceinline__ void row_loss_one(const RowParams& p, int64_t row) {
+  const float* r = p.row_stats + row * kRowStats;
+  bool ignored;
+  safe_label(p.labels[row], p.ignore_index, p.vocab_total, &ignored);
+  double ce_s = 0.0, ce_t = 0.0, div = 0.0;
+  if (!ignored) {
+    const double lse_s = (double)r[RS_MAX_S] + log((double)r[RS_SUM1_S]);
+    ce_s = lse_s - (double)r[RS_LABEL_S];
+    if (p.flags & F_TEACHER_CE) {
+      const double lse_t = (double)r[RS_MAX_T] + log((double)r[RS_SUM1_T]);
+      ce_t = lse_t - (double)r[RS_LABEL_T];
+    }
+    if (p.flags & F_KL) {
+      const double t = p.temperature, it = p.inv_t;
+      if (p.flags & F_JSD) {
+        div = p.row_sums[row * 2] * t * t;
+      } else {
+        const double lse_st = (double)r[RS_MAX_S] * it + log((double)r[RS_SUMT_S]);
+        const double lse_tt = (double)r[RS_MAX_T] * it + log((double)r[RS_SUMT_T]);
+        if (p.flags & F_KL_REVERSE) div = ((double)r[RS_CROSS] / r[RS_SUMT_S] - lse_st + lse_tt) * t * t;
+        else div = ((double)r[RS_CROSS] / r[RS_SUMT_T] - lse_tt + lse_st) * t * t;
       }
     }
-    p.row_losses[row] = (float)ce_s;
-    p.row_losses[p.ld_row_losses + row] = (float)ce_t;
-    p.row_losses[2 * p.ld_row_losses + row] = (float)div;
   }
+  p.row_losses[row] = (float)ce_s;
+  p.row_losses[p.ld_row_losses + row] = (float)ce_t;
+  p.row_losses[2 * p.ld_row_losses + row] = (float)div;
+}
+
+// One thread per row.
+__global__ void row_loss_kernel(RowParams p) {
+  for (int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; row < p.rows; row += (int64_t)gridDim.x * blockDim.x)
+    row_loss_one(p, row);
 }
 
 template <typename T>
@@ -215,15 +171,33 @@ __device__ __forceinline__ RowConsts row_consts(const RowParams& p, int64_t row)
   return c;
 }
 
+// The sweep kernels run one warp per row (no block-wide synchronisation); each lane handles vectors
+// of 8 consecutive vocabulary columns, 256 columns apart. Tile maxima are read from the [row][tile]
+// float2 array through the read-only cache (a warp touches at most two tiles per step).
+__device__ __forceinline__ const float2* row_tile_maxima(const RowParams& p, int64_t row) {
+  return reinterpret_cast<const float2*>(p.tile_stats) + row * p.n_vtiles;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+  return v;
+}
+
 // Loads 8 consecutive (student, teacher) values as offsets from the ROW maxima:
 //   ds = z - max_s ; dt = u - max_t
 template <typename WsT>
-__device__ __forceinline__ void load_row8(const RowParams& p, int64_t row, int64_t j0, const float* smax_s,
-                                          const float* smax_t, const RowConsts& c, bool need_t, float (&ds)[8],
-                                          float (&dt)[8]) {
-  const int tile = static_cast<int>(j0 / kVocabTile);
+__device__ __forceinline__ void load_row8(const RowParams& p, int64_t row, int64_t j0, const float2* tm,
+                                          const RowConsts& c, bool need_t, float (&ds)[8], float (&dt)[8]) {
+  const float2 m = __ldg(tm + j0 / kVocabTile);
   load8<WsT>(static_cast<const WsT*>(p.ws_s) + row * p.ld_ws + j0, ds);
-  const float off_s = smax_s[tile] - c.ms;
+  const float off_s = m.x - c.ms;
 #pragma unroll
   for (int j = 0; j < 8; ++j) ds[j] += off_s;
   if (need_t) {
@@ -232,7 +206,7 @@ __device__ __forceinline__ void load_row8(const RowParams& p, int64_t row, int64
       for (int j = 0; j < 8; ++j) dt[j] = (j0 + j < p.vocab) ? load_tg(p, row, j0 + j) - c.mt : 0.f;
     } else {
       load8<WsT>(static_cast<const WsT*>(p.ws_t) + row * p.ld_ws + j0, dt);
-      const float off_t = smax_t[tile] - c.mt;
+      const float off_t = m.y - c.mt;
 #pragma unroll
       for (int j = 0; j < 8; ++j) dt[j] += off_t;
     }
@@ -242,28 +216,132 @@ __device__ __forceinline__ void load_row8(const RowParams& p, int64_t row, int64
   }
 }
 
-__device__ __forceinline__ void load_tile_maxima(const RowParams& p, int64_t row, float* smax_s, float* smax_t) {
-  const float* rec = p.tile_stats + row * p.n_vtiles * kTileStats;
-  for (int i = threadIdx.x; i < p.n_vtiles; i += blockDim.x) {
-    smax_s[i] = rec[i * kTileStats + TS_MAX_S];
-    smax_t[i] = rec[i * kTileStats + TS_MAX_T];
-  }
-}
+// Teacher source of the row kernels (compile-time).
+enum TeacherSrc { TS_NONE = 0, TS_WS = 1, TS_GMEM = 2 };
+// Divergence kind of the gradient kernel (compile-time).
+enum DivKind { DK_NONE = 0, DK_FWD = 1, DK_REV = 2, DK_JSD = 3 };
 
-__device__ __forceinline__ float block_sum(float v, float* red) {
+// One warp per row: softmax statistics of this shard's part of the row, streamed from the shifted
+// logits in the workspace (and from the caller's teacher logits for a precomputed teacher):
+//   sum exp(z - M) and sum exp((z - M)/T) for the student and the teacher, and the divergence cross
+//   term (forward: sum exp((u - M_t)/T) (u - z)/T, reverse: sum exp((z - M_s)/T) (z - u)/T),
+// plus the exact label logits kept by the GEMM epilogue. Writes the row record (shard-local maxima).
+// Student / workspace-teacher maxima come from the epilogue's tile maxima; a caller-provided teacher
+// row is normalised on the fly (running maximum, rescaled sums). Each lane keeps two sets of
+// accumulators (even / odd columns) to shorten the dependency chains.
+template <typename WsT, int TSRC, bool TNO>
+__global__ void __launch_bounds__(256) row_stats_kernel(RowParams p) {
+  const uint32_t f = p.flags;
+  constexpr bool teacher = TSRC != TS_NONE;
+  const bool need_t1 = f & F_TEACHER_CE, kl = f & F_KL, rev = f & F_KL_REVERSE;
+  const float it = p.inv_t;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
+  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; row < p.rows; row += warps) {
+    const float2* tm = row_tile_maxima(p, row);
+    float lms = -CUDART_INF_F, lmt = -CUDART_INF_F;
+    for (int i = lane; i < p.n_vtiles; i += 32) {
+      const float2 m = __ldg(tm + i);
+      lms = fmaxf(lms, m.x);
+      lmt = fmaxf(lmt, m.y);
+    }
+    const float Ms = warp_max(lms);
+    float mt = (TSRC == TS_WS) ? warp_max(lmt) : -CUDART_INF_F;  // running maximum for a caller teacher
+    float s1s[2] = {0.f, 0.f}, sts[2] = {0.f, 0.f}, s1t[2] = {0.f, 0.f}, stt[2] = {0.f, 0.f}, cross[2] = {0.f, 0.f};
+    const WsT* rs = static_cast<const WsT*>(p.ws_s) + row * p.ld_ws;
+    const WsT* rt = static_cast<const WsT*>(p.ws_t) + row * p.ld_ws;
+    for (int64_t j0 = (int64_t)lane * 8; j0 < p.vocab; j0 += 256) {
+      const float2 m = __ldg(tm + j0 / kVocabTile);
+      float ds[8], u[8];
+      load8<WsT>(rs + j0, ds);
+      const int cnt = p.vocab - j0 < 8 ? static_cast<int>(p.vocab - j0) : 8;
+      if constexpr (TSRC == TS_GMEM) {
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) v += __shfl_down_sync(0xffffffffu, v, off);
-  const int w = threadIdx.x / 32, l = threadIdx.x % 32;
-  __syncthreads();
-  if (l == 0) red[w] = v;
-  __syncthreads();
-  float s = 0.f;
-  if (threadIdx.x < 32) {
-    s = (l < (int)(blockDim.x / 32)) ? red[l] : 0.f;
+        for (int j = 0; j < 8; ++j) u[j] = j < cnt ? load_tg(p, row, j0 + j) : -CUDART_INF_F;
+        float m8 = -CUDART_INF_F;
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) s += __shfl_down_sync(0xffffffffu, s, off);
+        for (int j = 0; j < 8; ++j) m8 = fmaxf(m8, u[j]);
+        if (m8 > mt) {  // rescale the teacher sums to the new running maximum
+          const float d = mt - m8;
+          const float f1 = __expf(d), ft = TNO ? __expf(d * it) : f1;
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            s1t[q] *= f1;
+            stt[q] *= ft;
+            if (!rev) cross[q] *= ft;
+          }
+          mt = m8;
+        }
+      } else if constexpr (TSRC == TS_WS) {
+        load8<WsT>(rt + j0, u);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) u[j] += m.y;  // raw teacher logit
+      }
+      const float off_s = m.x - Ms;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int q = j & 1;
+        const bool valid = j < cnt;
+        const float d = ds[j] + off_s;  // z - M_s
+        const float e1 = valid ? __expf(d) : 0.f;
+        const float et = TNO ? (valid ? __expf(d * it) : 0.f) : e1;
+        s1s[q] += e1;
+        sts[q] += et;
+        if constexpr (teacher) {
+          const float dt = u[j] - mt;
+          float e1t = 0.f, ett = 0.f;
+          if (valid) {
+            if (!TNO) {
+              e1t = __expf(dt);
+              ett = e1t;
+            } else {
+              if (need_t1) e1t = __expf(dt);
+              if (kl) ett = __expf(dt * it);
+            }
+          }
+          s1t[q] += e1t;
+          stt[q] += ett;
+          if (kl && valid) {
+            const float z = d + Ms;
+            cross[q] += rev ? et * (z - u[j]) * it : ett * (u[j] - z) * it;
+          }
+        }
+      }
+    }
+    const float cr = cross[0] + cross[1];
+    Partial ps{Ms, warp_sum(s1s[0] + s1s[1]), warp_sum(sts[0] + sts[1]), rev ? (double)warp_sum(cr) : 0.0};
+    Partial T{-CUDART_INF, 0.0, 0.0, 0.0};
+    if constexpr (TSRC == TS_GMEM) {
+      Partial pt{mt, s1t[0] + s1t[1], stt[0] + stt[1], rev ? 0.0 : (double)cr};
+      if (pt.max_v == -CUDART_INF) pt.sum1 = pt.sumt = pt.cross = 0.0;
+      T = warp_merge(pt, it, !rev);  // lane 0 holds the merge of the lanes' running maxima
+    } else if constexpr (TSRC == TS_WS) {
+      T = Partial{mt, warp_sum(s1t[0] + s1t[1]), warp_sum(stt[0] + stt[1]), rev ? 0.0 : (double)warp_sum(cr)};
+    }
+    if (lane == 0) {
+      float* out = p.row_stats + row * kRowStats;
+      bool ignored;
+      const int64_t ys = safe_label(p.labels[row], p.ignore_index, p.vocab_total, &ignored);
+      const bool has = !ignored && ys >= p.vocab_offset && ys < p.vocab_offset + p.vocab;
+      if (f & F_VALIDATE) {  // validate labels (debug profile): flag, never trap
+        const int64_t y = p.labels[row];
+        if (y != p.ignore_index && (y < 0 || y >= p.vocab_total)) atomicCAS(p.status, 0, ORDA_ERR_LABEL_RANGE);
+      }
+      out[RS_MAX_S] = (float)ps.max_v;
+      out[RS_SUM1_S] = (float)ps.sum1;
+      out[RS_SUMT_S] = (float)ps.sumt;
+      out[RS_MAX_T] = (float)T.max_v;
+      out[RS_SUM1_T] = (float)T.sum1;
+      out[RS_SUMT_T] = (float)T.sumt;
+      out[RS_CROSS] = (float)(rev ? ps.cross : T.cross);
+      out[RS_LABEL_S] = has ? p.label_logits[row * 2] : 0.f;
+      out[RS_LABEL_T] = has ? p.label_logits[row * 2 + 1] : 0.f;
+      out[RS_HAS_LABEL] = has ? 1.f : 0.f;
+      out[10] = rev ? 0.f : 1.f;  // cross term follows the teacher maxima
+      out[11] = p.inv_t;
+      for (int k = 12; k < kRowStats; ++k) out[k] = 0.f;
+    }
   }
-  return s;  // valid in thread 0
 }
 
 // log(exp(a) + exp(b)), stable.
@@ -273,25 +351,21 @@ __device__ __forceinline__ float log_add_exp(float a, float b) {
   return m + log1pf(__expf(-fabsf(a - b)));
 }
 
-// JSD (0 < beta < 1): per row, sum_j [b p_t (log p_t - log m) + (1-b) p_s (log p_s - log m)] and
-// sum_j p_s g_j with g = (1-b)(log p_s - log m); this shard's partial sums -> row_sums[row][0..1].
+// JSD (0 < beta < 1), one warp per row: sum_j [b p_t (log p_t - log m) + (1-b) p_s (log p_s - log m)]
+// and sum_j p_s g_j with g = (1-b)(log p_s - log m); this shard's partial sums -> row_sums[row][0..1].
 template <typename WsT>
-__global__ void jsd_sweep_kernel(RowParams p, float* row_sums) {
-  extern __shared__ float sh[];
-  float* smax_s = sh;
-  float* smax_t = sh + p.n_vtiles;
-  float* red = sh + 2 * p.n_vtiles;
+__global__ void __launch_bounds__(256) jsd_sweep_kernel(RowParams p, float* row_sums) {
   const float beta = p.jsd_beta, lb = logf(beta), l1b = log1pf(-beta), it = p.inv_t;
-  for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
-    __syncthreads();
-    load_tile_maxima(p, row, smax_s, smax_t);
-    __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
+  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; row < p.rows; row += warps) {
+    const float2* tm = row_tile_maxima(p, row);
     const RowConsts c = row_consts(p, row);
     float acc_j = 0.f, acc_g = 0.f;
     if (!c.ignored) {
-      for (int64_t j0 = (int64_t)threadIdx.x * 8; j0 < p.vocab; j0 += (int64_t)blockDim.x * 8) {
+      for (int64_t j0 = (int64_t)lane * 8; j0 < p.vocab; j0 += 256) {
         float ds[8], dt[8];
-        load_row8<WsT>(p, row, j0, smax_s, smax_t, c, true, ds, dt);
+        load_row8<WsT>(p, row, j0, tm, c, true, ds, dt);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           if (j0 + j >= p.vocab) break;
@@ -304,80 +378,125 @@ __global__ void jsd_sweep_kernel(RowParams p, float* row_sums) {
         }
       }
     }
-    const float sj = block_sum(acc_j, red);
-    const float sg = block_sum(acc_g, red);
-    if (threadIdx.x == 0) {
+    const float sj = warp_sum(acc_j), sg = warp_sum(acc_g);
+    if (lane == 0) {
       row_sums[row * 2] = sj;
       row_sums[row * 2 + 1] = sg;
     }
   }
 }
 
-// dlogits in place. Student:
+// dlogits in place, one warp per row. Student:
 //   w_s (softmax(z) - onehot) + w_kl * T * G,  G = p_s^T - p_t^T           (forward KL)
 //                                              G = p_s^T (a - R)             (reverse KL)
 //                                              G = p_s^T (g - sum p_s g)     (JSD)
 // Teacher (teacher CE only; the divergence never reaches the teacher): w_t (softmax(u) - onehot).
 // Ignored rows are zeroed.
-template <typename WsT>
-__global__ void grad_sweep_kernel(RowParams p) {
-  extern __shared__ float sh[];
-  float* smax_s = sh;
-  float* smax_t = sh + p.n_vtiles;
+template <typename WsT, int TSRC, int DK, bool TNO>
+__global__ void __launch_bounds__(256) grad_sweep_kernel(RowParams p) {
   const uint32_t f = p.flags;
-  const bool kl = f & F_KL, grad_t = f & F_GRAD_T, grad_s = f & F_GRAD_S;
-  const bool rev = f & F_KL_REVERSE, jsd = f & F_JSD;
+  constexpr bool kl = DK != DK_NONE;
+  const bool grad_t = f & F_GRAD_T, grad_s = f & F_GRAD_S;
   const float it = p.inv_t, kls = p.w_kl * p.temperature;
   const float beta = p.jsd_beta, lb = logf(fmaxf(beta, 1e-30f)), l1b = log1pf(-fminf(beta, 0.999999f));
-  for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
-    __syncthreads();
-    load_tile_maxima(p, row, smax_s, smax_t);
-    __syncthreads();
+  const bool need_t = TSRC != TS_NONE && (kl || grad_t);
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
+  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; row < p.rows; row += warps) {
+    const float2* tm = row_tile_maxima(p, row);
     const RowConsts c = row_consts(p, row);
     float rrev = 0.f, gsum = 0.f;
-    if (kl && rev) {
+    if (DK == DK_REV) {
       const float* r = p.row_stats + row * kRowStats;
       rrev = r[RS_CROSS] / r[RS_SUMT_S] - c.log_st - c.ms * it + c.log_tt + c.mt * it;
     }
-    if (kl && jsd) gsum = p.row_sums[row * 2 + 1];
+    if (DK == DK_JSD) gsum = p.row_sums[row * 2 + 1];
     WsT* rs = static_cast<WsT*>(p.ws_s) + row * p.ld_ws;
     WsT* rt = static_cast<WsT*>(p.ws_t) + row * p.ld_ws;
-    for (int64_t j0 = (int64_t)threadIdx.x * 8; j0 < p.vocab; j0 += (int64_t)blockDim.x * 8) {
+    for (int64_t j0 = (int64_t)lane * 8; j0 < p.vocab; j0 += 256) {
       float gs[8], gt[8];
       if (c.ignored) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) gs[j] = gt[j] = 0.f;
       } else {
         float ds[8], dt[8];
-        load_row8<WsT>(p, row, j0, smax_s, smax_t, c, kl || grad_t, ds, dt);
+        load_row8<WsT>(p, row, j0, tm, c, need_t, ds, dt);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const float onehot = (j0 + j == c.label_local) ? 1.f : 0.f;
           const float ps1 = __expf(ds[j] - c.log_s1);
           float g = p.w_s * (ps1 - onehot);
-          if (kl) {
+          // at T = 1 the tempered distributions are the CE softmaxes: reuse the exponentials
+          float pt1 = 0.f;
+          bool have_pt1 = false;
+          if constexpr (kl) {
             const float lps = ds[j] * it - c.log_st;
             const float lpt = dt[j] * it - c.log_tt;
-            const float ps = __expf(lps);
+            const float ps = TNO ? __expf(lps) : ps1;
             float d;
-            if (jsd) {
+            if constexpr (DK == DK_JSD) {
               const float lm = log_add_exp(lb + lpt, l1b + lps);
               d = ps * ((1.f - beta) * (lps - lm) - gsum);
-            } else if (rev) {
+            } else if constexpr (DK == DK_REV) {
               d = ps * ((lps - lpt) - rrev);
             } else {
-              d = ps - __expf(lpt);
+              const float pt = __expf(lpt);
+              if (!TNO) {
+                pt1 = pt;
+                have_pt1 = true;
+              }
+              d = ps - pt;
             }
             g += kls * d;
           }
           gs[j] = g;
-          gt[j] = grad_t ? p.w_t * (__expf(dt[j] - c.log_t1) - onehot) : 0.f;
+          if (TSRC != TS_NONE && grad_t) {
+            if (!have_pt1) pt1 = __expf(dt[j] - c.log_t1);
+            gt[j] = p.w_t * (pt1 - onehot);
+          } else {
+            gt[j] = 0.f;
+          }
         }
       }
       if (grad_s) store8<WsT>(rs + j0, gs);
       if (grad_t) store8<WsT>(rt + j0, gt);
     }
   }
+}
+
+// Launch helpers selecting the compile-time specialisation from the runtime flags.
+template <typename WsT, int TSRC>
+void launch_row_stats_t(const RowParams& r, int grid, cudaStream_t s) {
+  if (r.flags & F_T_NOT_ONE) row_stats_kernel<WsT, TSRC, true><<<grid, 256, 0, s>>>(r);
+  else row_stats_kernel<WsT, TSRC, false><<<grid, 256, 0, s>>>(r);
+}
+
+template <typename WsT>
+void launch_row_stats(const RowParams& r, int grid, cudaStream_t s) {
+  if (!(r.flags & F_TEACHER)) launch_row_stats_t<WsT, TS_NONE>(r, grid, s);
+  else if (r.flags & F_TEACHER_GMEM) launch_row_stats_t<WsT, TS_GMEM>(r, grid, s);
+  else launch_row_stats_t<WsT, TS_WS>(r, grid, s);
+}
+
+template <typename WsT, int TSRC, int DK>
+void launch_grad_sweep_dk(const RowParams& r, int grid, cudaStream_t s) {
+  if (r.flags & F_T_NOT_ONE) grad_sweep_kernel<WsT, TSRC, DK, true><<<grid, 256, 0, s>>>(r);
+  else grad_sweep_kernel<WsT, TSRC, DK, false><<<grid, 256, 0, s>>>(r);
+}
+
+template <typename WsT, int TSRC>
+void launch_grad_sweep_t(const RowParams& r, int grid, cudaStream_t s) {
+  if (!(r.flags & F_KL)) launch_grad_sweep_dk<WsT, TSRC, DK_NONE>(r, grid, s);
+  else if (r.flags & F_JSD) launch_grad_sweep_dk<WsT, TSRC, DK_JSD>(r, grid, s);
+  else if (r.flags & F_KL_REVERSE) launch_grad_sweep_dk<WsT, TSRC, DK_REV>(r, grid, s);
+  else launch_grad_sweep_dk<WsT, TSRC, DK_FWD>(r, grid, s);
+}
+
+template <typename WsT>
+void launch_grad_sweep(const RowParams& r, int grid, cudaStream_t s) {
+  if (!(r.flags & F_TEACHER)) launch_grad_sweep_t<WsT, TS_NONE>(r, grid, s);
+  else if (r.flags & F_TEACHER_GMEM) launch_grad_sweep_t<WsT, TS_GMEM>(r, grid, s);
+  else launch_grad_sweep_t<WsT, TS_WS>(r, grid, s);
 }
 
 // Single block: reduce per-row losses (double) into the reference's scalars

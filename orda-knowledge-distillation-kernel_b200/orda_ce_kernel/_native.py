@@ -92,6 +92,7 @@ EXPORTED_SYMBOLS = (
     "orda_shard_jsd_partials",
     "orda_shard_backward",
     "orda_debug_gemm",
+    "orda_debug_gemm_pair",
 )
 
 _lib = None
@@ -127,6 +128,8 @@ def _declare(lib):
     lib.orda_shard_backward.argtypes = [P, _vp, ctypes.c_size_t, _vp, _vp, _vp]
     lib.orda_debug_gemm.restype = _i32
     lib.orda_debug_gemm.argtypes = [_i32, _i32, _i32, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _vp, _vp]
+    lib.orda_debug_gemm_pair.restype = _i32
+    lib.orda_debug_gemm_pair.argtypes = lib.orda_debug_gemm.argtypes
 
 
 def load(path: str | None = None):
