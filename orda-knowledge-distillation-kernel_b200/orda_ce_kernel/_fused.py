@@ -99,105 +99,128 @@ def _check_labels(labels: torch.Tensor, vocab: int, ignore_index: int) -> None:
         )
 
 
+class Prepared:
+    """Arguments of one library call plus the tensors that must outlive it."""
+
+    __slots__ = ("args", "keep", "g_hs", "g_ht", "g_w", "g_wt", "out", "status", "h", "h_t", "dev")
+
+
+def prepare_call(student_hidden, teacher_hidden, weight, teacher_weight, labels, teacher_logits, spec: FusedSpec,
+                 vocab_offset: int = 0, vocab_total: int | None = None) -> Prepared:
+    """Operands in the compute dtype (the reference's rule), TMA-friendly layout, output buffers and
+    the filled ``orda_distill_args_t``. ``weight`` (and a separate teacher's weight) may be a vocab
+    shard starting at ``vocab_offset`` of a ``vocab_total``-row lm_head."""
+    mode = spec.mode
+    dev = student_hidden.device
+    if dev.type != "cuda":
+        raise RuntimeError("the fused distillation kernels need CUDA tensors (there is no CPU fallback)")
+    kl_on = spec.kl_weight != 0.0
+    tied, sep = mode == "tied", mode == "separate"
+    t_logits_mode, t_hidden_mode = mode == "precomputed_logits", mode == "precomputed_hidden"
+
+    # ---- compute dtype, as each reference Function picks it
+    if tied:
+        cdt = default_compute_dtype(weight, student_hidden, teacher_hidden)
+    elif sep:
+        cdt = default_compute_dtype(weight, teacher_weight, student_hidden, teacher_hidden)
+    elif t_logits_mode:
+        cdt = default_compute_dtype(weight, student_hidden, teacher_logits) if kl_on else default_compute_dtype(weight, student_hidden)
+    else:
+        cdt = default_compute_dtype(weight, student_hidden, teacher_hidden) if kl_on else default_compute_dtype(weight, student_hidden)
+    if cdt not in _DTYPE_CODE:
+        cdt = torch.float32
+
+    need_hs = bool(student_hidden.requires_grad)
+    need_w = bool(weight.requires_grad)
+    need_ht = bool(teacher_hidden is not None and teacher_hidden.requires_grad and (tied or (sep and spec.teacher_ce_weight > 0)))
+    need_wt = bool(sep and spec.teacher_ce_weight > 0 and teacher_weight is not None and teacher_weight.requires_grad)
+
+    n, h = student_hidden.shape
+    vocab = weight.shape[0]
+    is16 = cdt != torch.float32
+    hp = _round8(h) if is16 else h
+    hs_c = _operand(student_hidden.detach(), cdt, hp)
+    w_c = _operand(weight.detach(), cdt, hp)
+    ht_c = wt_c = tl_c = None
+    h_t = h
+    if tied:
+        ht_c = _operand(teacher_hidden.detach(), cdt, hp)
+        h_t = h
+    elif sep or t_hidden_mode:
+        h_t = teacher_hidden.shape[1]
+        htp = _round8(h_t) if is16 else h_t
+        ht_c = _operand(teacher_hidden.detach(), cdt, htp)
+        wt_c = _operand(teacher_weight.detach(), cdt, htp)
+    elif t_logits_mode:
+        tl_c = teacher_logits.detach()
+        if tl_c.dtype not in _DTYPE_CODE:
+            tl_c = tl_c.float()
+        if tl_c.stride(1) != 1:
+            tl_c = tl_c.contiguous()
+    h_tp = ht_c.shape[1] if ht_c is not None else hp
+    labels_c = labels.contiguous()
+    if spec.validate_labels:
+        _check_labels(labels_c, vocab if vocab_total is None else int(vocab_total), spec.ignore_index)
+
+    f32_acc = spec.fp32_grad_weight or not is16
+    wdt = torch.float32 if f32_acc else cdt
+    g_hs = torch.empty((n, hp), dtype=cdt, device=dev) if need_hs else None
+    g_w = torch.empty((vocab, hp), dtype=wdt, device=dev) if need_w else None
+    g_ht = torch.empty((n, h_tp), dtype=cdt, device=dev) if need_ht else None
+    g_wt = torch.empty((vocab, h_tp), dtype=wdt, device=dev) if need_wt else None
+    out = torch.empty(_native.OUT_SLOTS, dtype=torch.float32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    a = _native.DistillArgs()
+    a.abi_version = _native.ABI_VERSION
+    a.teacher_mode = _MODE_CODE[mode]
+    a.compute_dtype = _DTYPE_CODE[cdt]
+    a.teacher_logits_dtype = _DTYPE_CODE[tl_c.dtype] if tl_c is not None else _native.F32
+    a.n_rows, a.hidden, a.teacher_hidden, a.vocab = n, hp, h_tp, vocab
+    a.vocab_offset = int(vocab_offset)
+    a.vocab_total = int(vocab if vocab_total is None else vocab_total)
+    a.student_hidden, a.ld_student_hidden = _ptr(hs_c), hs_c.stride(0)
+    a.weight, a.ld_weight = _ptr(w_c), w_c.stride(0)
+    if ht_c is not None:
+        a.teacher_hidden_ptr, a.ld_teacher_hidden = _ptr(ht_c), ht_c.stride(0)
+    if wt_c is not None:
+        a.teacher_weight, a.ld_teacher_weight = _ptr(wt_c), wt_c.stride(0)
+    if tl_c is not None:
+        a.teacher_logits, a.ld_teacher_logits = _ptr(tl_c), tl_c.stride(0)
+    a.labels = _ptr(labels_c)
+    a.student_ce_weight = float(spec.student_ce_weight)
+    a.teacher_ce_weight = float(spec.teacher_ce_weight)
+    a.kl_weight = float(spec.kl_weight)
+    a.kl_temperature = float(spec.kl_temperature)
+    a.jsd_beta = float(spec.jsd_beta)
+    a.divergence = _DIV_CODE[spec.divergence]
+    a.ignore_index = int(spec.ignore_index)
+    a.reduction = _native.REDUCTION_MEAN if spec.reduction == "mean" else _native.REDUCTION_SUM
+    a.validate_labels = 0
+    a.need_grad_student_hidden, a.need_grad_weight = int(need_hs), int(need_w)
+    a.need_grad_teacher_hidden, a.need_grad_teacher_weight = int(need_ht), int(need_wt)
+    a.chunk_rows = int(spec.chunk_rows)
+    a.out_reduced = _ptr(out)
+    a.out_row_losses = None
+    a.grad_student_hidden, a.grad_weight = _ptr(g_hs), _ptr(g_w)
+    a.grad_teacher_hidden, a.grad_teacher_weight = _ptr(g_ht), _ptr(g_wt)
+    a.grad_weight_fp32 = int(f32_acc)
+    a.device_status = _ptr(status)
+
+    pr = Prepared()
+    pr.args, pr.keep = a, (hs_c, w_c, ht_c, wt_c, tl_c, labels_c)
+    pr.g_hs, pr.g_ht, pr.g_w, pr.g_wt = g_hs, g_ht, g_w, g_wt
+    pr.out, pr.status, pr.h, pr.h_t, pr.dev = out, status, h, h_t, dev
+    return pr
+
+
 class FusedDistillFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, student_hidden, teacher_hidden, weight, teacher_weight, labels, teacher_logits, spec: FusedSpec):
         lib = _native.load()
-        mode = spec.mode
-        dev = student_hidden.device
-        if dev.type != "cuda":
-            raise RuntimeError("the fused distillation kernels need CUDA tensors (there is no CPU fallback)")
-        kl_on = spec.kl_weight != 0.0
-        tied, sep = mode == "tied", mode == "separate"
-        t_logits_mode, t_hidden_mode = mode == "precomputed_logits", mode == "precomputed_hidden"
-
-        # ---- compute dtype, as each reference Function picks it
-        if tied:
-            cdt = default_compute_dtype(weight, student_hidden, teacher_hidden)
-        elif sep:
-            cdt = default_compute_dtype(weight, teacher_weight, student_hidden, teacher_hidden)
-        elif t_logits_mode:
-            cdt = default_compute_dtype(weight, student_hidden, teacher_logits) if kl_on else default_compute_dtype(weight, student_hidden)
-        else:
-            cdt = default_compute_dtype(weight, student_hidden, teacher_hidden) if kl_on else default_compute_dtype(weight, student_hidden)
-        if cdt not in _DTYPE_CODE:
-            cdt = torch.float32
-
-        need_hs = bool(student_hidden.requires_grad)
-        need_w = bool(weight.requires_grad)
-        need_ht = bool(teacher_hidden is not None and teacher_hidden.requires_grad and (tied or (sep and spec.teacher_ce_weight > 0)))
-        need_wt = bool(sep and spec.teacher_ce_weight > 0 and teacher_weight is not None and teacher_weight.requires_grad)
-
-        n, h = student_hidden.shape
-        vocab = weight.shape[0]
-        is16 = cdt != torch.float32
-        hp = _round8(h) if is16 else h
-        hs_c = _operand(student_hidden.detach(), cdt, hp)
-        w_c = _operand(weight.detach(), cdt, hp)
-        ht_c = wt_c = tl_c = None
-        h_t = h
-        if tied:
-            ht_c = _operand(teacher_hidden.detach(), cdt, hp)
-            h_t = h
-        elif sep or t_hidden_mode:
-            h_t = teacher_hidden.shape[1]
-            htp = _round8(h_t) if is16 else h_t
-            ht_c = _operand(teacher_hidden.detach(), cdt, htp)
-            wt_c = _operand(teacher_weight.detach(), cdt, htp)
-        elif t_logits_mode:
-            tl_c = teacher_logits.detach()
-            if tl_c.dtype not in _DTYPE_CODE:
-                tl_c = tl_c.float()
-            if tl_c.stride(1) != 1:
-                tl_c = tl_c.contiguous()
-        h_tp = ht_c.shape[1] if ht_c is not None else hp
-        labels_c = labels.contiguous()
-        if spec.validate_labels:
-            _check_labels(labels_c, vocab, spec.ignore_index)
-
-        f32_acc = spec.fp32_grad_weight or not is16
-        wdt = torch.float32 if f32_acc else cdt
-        g_hs = torch.empty((n, hp), dtype=cdt, device=dev) if need_hs else None
-        g_w = torch.empty((vocab, hp), dtype=wdt, device=dev) if need_w else None
-        g_ht = torch.empty((n, h_tp), dtype=cdt, device=dev) if need_ht else None
-        g_wt = torch.empty((vocab, h_tp), dtype=wdt, device=dev) if need_wt else None
-        out = torch.empty(_native.OUT_SLOTS, dtype=torch.float32, device=dev)
-        status = torch.zeros(1, dtype=torch.int32, device=dev)
-
-        a = _native.DistillArgs()
-        a.abi_version = _native.ABI_VERSION
-        a.teacher_mode = _MODE_CODE[mode]
-        a.compute_dtype = _DTYPE_CODE[cdt]
-        a.teacher_logits_dtype = _DTYPE_CODE[tl_c.dtype] if tl_c is not None else _native.F32
-        a.n_rows, a.hidden, a.teacher_hidden, a.vocab = n, hp, h_tp, vocab
-        a.vocab_offset, a.vocab_total = 0, vocab
-        a.student_hidden, a.ld_student_hidden = _ptr(hs_c), hs_c.stride(0)
-        a.weight, a.ld_weight = _ptr(w_c), w_c.stride(0)
-        if ht_c is not None:
-            a.teacher_hidden_ptr, a.ld_teacher_hidden = _ptr(ht_c), ht_c.stride(0)
-        if wt_c is not None:
-            a.teacher_weight, a.ld_teacher_weight = _ptr(wt_c), wt_c.stride(0)
-        if tl_c is not None:
-            a.teacher_logits, a.ld_teacher_logits = _ptr(tl_c), tl_c.stride(0)
-        a.labels = _ptr(labels_c)
-        a.student_ce_weight = float(spec.student_ce_weight)
-        a.teacher_ce_weight = float(spec.teacher_ce_weight)
-        a.kl_weight = float(spec.kl_weight)
-        a.kl_temperature = float(spec.kl_temperature)
-        a.jsd_beta = float(spec.jsd_beta)
-        a.divergence = _DIV_CODE[spec.divergence]
-        a.ignore_index = int(spec.ignore_index)
-        a.reduction = _native.REDUCTION_MEAN if spec.reduction == "mean" else _native.REDUCTION_SUM
-        a.validate_labels = 0
-        a.need_grad_student_hidden, a.need_grad_weight = int(need_hs), int(need_w)
-        a.need_grad_teacher_hidden, a.need_grad_teacher_weight = int(need_ht), int(need_wt)
-        a.chunk_rows = int(spec.chunk_rows)
-        a.out_reduced = _ptr(out)
-        a.out_row_losses = None
-        a.grad_student_hidden, a.grad_weight = _ptr(g_hs), _ptr(g_w)
-        a.grad_teacher_hidden, a.grad_teacher_weight = _ptr(g_ht), _ptr(g_wt)
-        a.grad_weight_fp32 = int(f32_acc)
-        a.device_status = _ptr(status)
+        pr = prepare_call(student_hidden, teacher_hidden, weight, teacher_weight, labels, teacher_logits, spec)
+        a, dev, out, status = pr.args, pr.dev, pr.out, pr.status
+        g_hs, g_ht, g_w, g_wt, h_t = pr.g_hs, pr.g_ht, pr.g_w, pr.g_wt, pr.h_t
 
         hooks = getattr(_HOOKS, "value", None)
         if hooks is not None:

@@ -1,0 +1,197 @@
+"""Multi-GPU forms of the distillation loss (one process per GPU, ``torch.distributed`` over NCCL).
+
+The reference has no distributed code; both forms here are additions that keep the single-GPU
+semantics of ``distillation_loss`` (same losses, same gradients as one process holding every row and
+the whole lm_head).
+
+* Token sharding (:func:`token_parallel_distillation_loss`): every rank holds its own rows and a full
+  lm_head replica. The fused kernel runs on the local rows with sum reduction; the loss sums and the
+  non-ignored label count are all-reduced (a few bytes) so the returned loss and every gradient use the
+  GLOBAL mean. The lm_head gradient of each rank is its local contribution: sum it over ranks (DDP does,
+  or :func:`allreduce_weight_grad`).
+
+* Vocab sharding (:func:`vocab_parallel_distillation_loss`): every rank holds all rows and a slice of
+  the lm_head rows (vocab ids ``vocab_offset .. vocab_offset + V_local``). Each rank computes the softmax
+  statistics of its slice; the per-row records (16 floats per row) are all-gathered and LSE-merged, so
+  every rank sees the global log-sum-exps (for JSD the two per-row partial sums are all-reduced as
+  well). Each rank then writes its dlogits, its complete lm_head-slice gradient (no communication) and
+  a partial hidden-state gradient that is all-reduced.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+from torch.autograd.function import once_differentiable
+
+from . import _native
+from ._fused import FusedSpec, prepare_call
+from .api import (
+    DistillationLossOutput,
+    PrecomputedTeacher,
+    SeparateTeacher,
+    TiedTeacher,
+    _resolve_teacher_ce_weight,
+    _teacher_mode_and_tensors,
+    distillation_loss,
+)
+from .ops._common import check_divergence
+
+
+# ---------------------------------------------------------------------------------- token sharding
+def token_parallel_distillation_loss(student_hidden, weight, labels, teacher, *, group=None, reduction="mean",
+                                     _local_loss=None, **kwargs) -> DistillationLossOutput:
+    """``distillation_loss`` over the rows of all ranks in ``group``; this rank passes its own rows.
+
+    Returns the global loss and components (identical on every rank). Gradients w.r.t. this rank's
+    hidden states are final; the lm_head gradient is this rank's share of the global gradient.
+    ``_local_loss`` replaces the per-rank loss call (tests inject a CPU formula).
+    """
+    if reduction not in ("mean", "sum"):
+        raise ValueError(f"reduction must be 'mean' or 'sum', got {reduction!r}")
+    local = _local_loss or distillation_loss
+    out = local(student_hidden, weight, labels, teacher, reduction="sum", **kwargs)
+    ignore_index = kwargs.get("ignore_index", -100)
+    count = (labels != ignore_index).sum().to(torch.float32)
+    stats = torch.stack([out.loss.detach().float(), out.student_ce.float(), out.teacher_ce.float(),
+                         out.kl.float(), count.to(out.loss.device)])
+    dist.all_reduce(stats, group=group)
+    inv = 1.0 / torch.clamp(stats[4], min=1.0) if reduction == "mean" else torch.ones((), device=stats.device)
+    # global loss: this rank's sum carries the gradient, the other ranks' sums are constants
+    loss = out.loss * inv + (stats[0] - out.loss.detach()) * inv
+    return DistillationLossOutput(loss, stats[1] * inv, stats[2] * inv, stats[3] * inv)
+
+
+def allreduce_weight_grad(weight: torch.Tensor, group=None, async_op: bool = False):
+    """Sum ``weight.grad`` over the ranks of ``group`` (token-sharded data parallelism)."""
+    if weight.grad is None:
+        return None
+    return dist.all_reduce(weight.grad, group=group, async_op=async_op)
+
+
+# ---------------------------------------------------------------------------------- vocab sharding
+class _NativeShardOps:
+    """The C-ABI phases of one vocab shard (include/orda_b200.h, orda_shard_*)."""
+
+    def __init__(self):
+        self.lib = _native.load()
+
+    def forward(self, pr):
+        lib = self.lib
+        n = pr.args.n_rows
+        ws_bytes = int(lib.orda_shard_workspace_bytes(pr.args))
+        self.ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=pr.dev)
+        self.ws_bytes = ws_bytes
+        self.stream = torch.cuda.current_stream(pr.dev).cuda_stream
+        rs = torch.empty((n, _native.ROW_STATS), dtype=torch.float32, device=pr.dev)
+        _native.check(lib.orda_shard_forward(pr.args, self.ws.data_ptr(), ws_bytes, rs.data_ptr(), self.stream),
+                      "orda_shard_forward")
+        return rs
+
+    def merge(self, gathered, world, n):
+        rs = torch.empty((n, _native.ROW_STATS), dtype=torch.float32, device=gathered.device)
+        _native.check(self.lib.orda_merge_row_stats(gathered.data_ptr(), world, n, rs.data_ptr(), self.stream),
+                      "orda_merge_row_stats")
+        return rs
+
+    def jsd_partials(self, pr, row_stats):
+        sums = torch.empty((pr.args.n_rows, 2), dtype=torch.float32, device=pr.dev)
+        _native.check(self.lib.orda_shard_jsd_partials(pr.args, self.ws.data_ptr(), self.ws_bytes, row_stats.data_ptr(),
+                                                        sums.data_ptr(), self.stream), "orda_shard_jsd_partials")
+        return sums
+
+    def backward(self, pr, row_stats, row_sums):
+        _native.check(self.lib.orda_shard_backward(pr.args, self.ws.data_ptr(), self.ws_bytes, row_stats.data_ptr(),
+                                                   None if row_sums is None else row_sums.data_ptr(), self.stream),
+                      "orda_shard_backward")
+
+
+class _VocabShardFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, student_hidden, teacher_hidden, weight, teacher_weight, labels, teacher_logits, spec,
+                vocab_offset, vocab_total, group):
+        world = dist.get_world_size(group)
+        pr = prepare_call(student_hidden, teacher_hidden, weight, teacher_weight, labels, teacher_logits, spec,
+                          vocab_offset=vocab_offset, vocab_total=vocab_total)
+        ops = _NativeShardOps()
+        n = pr.args.n_rows
+        local = ops.forward(pr)
+        gathered = torch.empty((world, n, _native.ROW_STATS), dtype=torch.float32, device=pr.dev)
+        dist.all_gather_into_tensor(gathered, local, group=group)
+        row_stats = ops.merge(gathered, world, n)
+        row_sums = None
+        jsd = spec.kl_weight != 0.0 and spec.divergence == "jsd" and 0.0 < spec.jsd_beta < 1.0
+        if jsd:
+            row_sums = ops.jsd_partials(pr, row_stats)
+            dist.all_reduce(row_sums, group=group)
+        ops.backward(pr, row_stats, row_sums)
+        # the hidden-state gradients are sums over the vocab shards
+        for g in (pr.g_hs, pr.g_ht):
+            if g is not None:
+                dist.all_reduce(g, group=group)
+        out = pr.out
+        loss = out[_native.OUT_LOSS].clone()
+        ce_s, ce_t, kl = (out[i].clone() for i in (_native.OUT_STUDENT_CE, _native.OUT_TEACHER_CE, _native.OUT_KL))
+        ctx.save_for_backward(pr.g_hs, pr.g_ht, pr.g_w, pr.g_wt, out[_native.OUT_MEAN_SCALE].clone())
+        ctx.shapes = (student_hidden.shape[1], pr.h_t)
+        ctx.dtypes = (student_hidden.dtype, teacher_hidden.dtype if teacher_hidden is not None else None,
+                      weight.dtype, teacher_weight.dtype if teacher_weight is not None else None)
+        ctx.mark_non_differentiable(ce_s, ce_t, kl)
+        return loss, ce_s, ce_t, kl
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad_output, *_):
+        g_hs, g_ht, g_w, g_wt, mean_scale = ctx.saved_tensors
+        if grad_output is None:
+            return (None,) * 10
+        h, h_t = ctx.shapes
+        dt_hs, dt_ht, dt_w, dt_wt = ctx.dtypes
+        eff = grad_output.to(torch.float32) * mean_scale
+
+        def scale(g, cols, dtype):
+            if g is None:
+                return None
+            if g.shape[1] != cols:
+                g = g[:, :cols]
+            return (g * eff).to(dtype)
+
+        return (scale(g_hs, h, dt_hs), scale(g_ht, h_t, dt_ht), scale(g_w, h, dt_w), scale(g_wt, h_t, dt_wt),
+                None, None, None, None, None, None)
+
+
+def vocab_parallel_distillation_loss(student_hidden, weight_shard, labels, teacher, *, vocab_offset: int,
+                                     vocab_total: int, group=None, student_ce_weight: float = 1.0,
+                                     teacher_ce_weight: float | None = None, kl_weight: float = 0.0,
+                                     kl_temperature: float = 1.0, ignore_index: int = -100, reduction: str = "mean",
+                                     kl_divergence: str = "forward", jsd_beta: float = 0.5,
+                                     fp32_grad_weight_accumulation: bool = False) -> DistillationLossOutput:
+    """``distillation_loss`` with the lm_head split by vocabulary rows across the ranks of ``group``.
+
+    ``weight_shard`` holds vocab ids ``[vocab_offset, vocab_offset + weight_shard.shape[0])`` of a
+    ``vocab_total``-row lm_head; a ``SeparateTeacher`` carries the same slice of the teacher lm_head and a
+    ``PrecomputedTeacher(logits=...)`` the same columns of the teacher logits. Every rank passes all rows
+    and the same labels (global vocab ids). Returns the global loss (identical on every rank); the
+    gradient of ``weight_shard`` is the complete gradient of that slice.
+    """
+    if reduction not in ("mean", "sum"):
+        raise ValueError(f"reduction must be 'mean' or 'sum', got {reduction!r}")
+    if kl_temperature <= 0.0:
+        raise ValueError(f"kl_temperature must be > 0.0, got {kl_temperature}")
+    check_divergence(kl_divergence, jsd_beta)
+    mode, th, tw, tl = _teacher_mode_and_tensors(teacher)
+    tce = _resolve_teacher_ce_weight(mode, teacher_ce_weight)
+    if mode == "precomputed":
+        if tce != 0.0:
+            raise ValueError("PrecomputedTeacher requires teacher_ce_weight=0.0")
+        mode = "precomputed_logits" if tl is not None else "precomputed_hidden"
+    if not (0 <= vocab_offset and vocab_offset + weight_shard.shape[0] <= vocab_total):
+        raise ValueError("weight_shard must lie inside [0, vocab_total)")
+    spec = FusedSpec(mode=mode, student_ce_weight=float(student_ce_weight), teacher_ce_weight=float(tce),
+                     kl_weight=float(kl_weight), kl_temperature=float(kl_temperature), ignore_index=int(ignore_index),
+                     reduction=reduction, divergence=kl_divergence, jsd_beta=float(jsd_beta),
+                     fp32_grad_weight=bool(fp32_grad_weight_accumulation))
+    if isinstance(teacher, (TiedTeacher, SeparateTeacher, PrecomputedTeacher)) is False:
+        raise TypeError("teacher must be TiedTeacher, SeparateTeacher, or PrecomputedTeacher")
+    out = _VocabShardFunction.apply(student_hidden, th, weight_shard, tw, labels, tl, spec, int(vocab_offset),
+                                    int(vocab_total), group)
+    return DistillationLossOutput(*out)
