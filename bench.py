@@ -344,7 +344,7 @@ def run_ours(args):
     peak_tf, peak_hbm, peak_src = _peaks()
     achieved = flops_tok[dom] * rows / (phase_ms[dom] / 1e3) / 1e12
     total_flops_tok = 10.0 * HID * VOCAB
-    step_tf = total_flops_tok * rows / (ms / 1e3) / 1e12
+    step_tf = total_flops_tok * rows / (ms / 1e3) / 1e12  # per GPU: each rank runs `rows` tokens
     traffic = _profile_traffic().get(str(dom))
 
     # ---------------- end-to-end through the public API with host buffers
@@ -400,8 +400,8 @@ def run_ours(args):
                 "parallelism": f"token-sharded dp{world}" if world > 1 else "single GPU",
                 "l2": "inputs larger than L2 (lm_head 1.05 GB, logits workspace 4.2 GB)",
             },
-            "tflops_per_gpu": step_tf / world if world > 1 else step_tf,
-            "frac_of_bf16_peak_step": (step_tf / world) / peak_tf,
+            "tflops_per_gpu": step_tf,
+            "frac_of_bf16_peak_step": step_tf / peak_tf,
             "phase_ms": {names[p]: phase_ms[p] for p in range(_native.PHASES)},
             "roofline": {"bound": "tensor", "kernel": names[dom], "achieved": achieved, "peak": peak_tf,
                          "unit": "TFLOP/s", "frac": achieved / peak_tf, "peak_source": peak_src,

@@ -132,7 +132,8 @@ typedef struct orda_distill_args {
   void* dweight_done_event;     /* cudaEvent_t recorded once the weight gradients are complete, so a
                                    caller can start their all-reduce on another stream                 */
   int32_t dweight_first;        /* run the dW GEMMs before the dH GEMMs (overlap the dW all-reduce)  */
-  int32_t reserved0;
+  int32_t grads_include_mean_scale; /* 1: gradients already include out_reduced[ORDA_OUT_MEAN_SCALE]
+                                   (1/count for mean), so backward only multiplies by grad_output     */
 } orda_distill_args_t;
 
 /* phases bracketed by phase_events */
@@ -150,6 +151,11 @@ size_t orda_args_struct_size(void);
 
 /* Number of kernels this library has launched in this process (monotonic; for launch accounting). */
 uint64_t orda_kernel_launches(void);
+
+/* In-place backward rescale of a gradient buffer: data[i] *= *scale (device fp32 scalar), skipped
+ * entirely on the device when *scale == 1. dtype: ORDA_F32 / ORDA_F16 / ORDA_BF16. Replaces the
+ * elementwise rescale of the reference's backward (ops/tied_teacher.py:538-545). */
+int32_t orda_scale_grad(void* data, int64_t n, int32_t dtype, const float* scale, void* stream);
 
 /* Human-readable text for a status code. */
 const char* orda_status_string(int32_t status);

@@ -252,6 +252,7 @@ RowParams row_params(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, c
   r.ws_s = ws + P.off_ws_s; r.ws_t = ws + P.off_ws_t; r.ld_ws = P.vpad;
   r.t_gmem = c.tg; r.ld_tg = a->ld_teacher_logits; r.tg_dtype = a->teacher_logits_dtype;
   r.status = a->device_status;
+  r.grad_scale = a->grads_include_mean_scale ? a->out_reduced + ORDA_OUT_MEAN_SCALE : nullptr;
   return r;
 }
 
@@ -526,6 +527,10 @@ int check_operands(const orda_distill_args_t* a, const Plan& P) {
 template <typename WsT>
 int run_all(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, cudaStream_t s) {
   int rc;
+  if (a->grads_include_mean_scale) {
+    count_launch();
+    mean_scale_kernel<<<1, 1024, 0, s>>>(a->labels, a->n_rows, a->ignore_index, a->reduction, a->out_reduced);
+  }
   for (int64_t r0 = 0; r0 < a->n_rows; r0 += P.C) {
     const int64_t rows = std::min<int64_t>(P.C, a->n_rows - r0);
     const ChunkPtrs c = chunk_ptrs(a, r0, rows);
@@ -564,6 +569,21 @@ int32_t orda_abi_version(void) { return ORDA_ABI_VERSION; }
 uint64_t orda_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
 
 size_t orda_args_struct_size(void) { return sizeof(orda_distill_args_t); }
+
+int32_t orda_scale_grad(void* data, int64_t n, int32_t dtype, const float* scale, void* stream) {
+  if (!data || !scale || n < 0) return ORDA_ERR_INVALID_ARGUMENT;
+  if (n == 0) return ORDA_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = static_cast<int>(std::min<int64_t>(cdiv(n, 8 * 256), 8 * num_sms()));
+  count_launch();
+  switch (dtype) {
+    case ORDA_BF16: scale_grad_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<__nv_bfloat16*>(data), n, scale); break;
+    case ORDA_F16: scale_grad_kernel<__half><<<grid, 256, 0, s>>>(static_cast<__half*>(data), n, scale); break;
+    case ORDA_F32: scale_grad_kernel<float><<<grid, 256, 0, s>>>(static_cast<float*>(data), n, scale); break;
+    default: return ORDA_ERR_INVALID_ARGUMENT;
+  }
+  return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
+}
 
 const char* orda_status_string(int32_t status) {
   switch (status) {
@@ -661,6 +681,11 @@ int32_t orda_shard_backward(const orda_distill_args_t* args, void* workspace, si
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const ChunkPtrs c = chunk_ptrs(args, 0, args->n_rows);
+  if (args->grads_include_mean_scale) {
+    count_launch();
+    mean_scale_kernel<<<1, 1024, 0, s>>>(args->labels, args->n_rows, args->ignore_index, args->reduction,
+                                         args->out_reduced);
+  }
   switch (args->compute_dtype) {
     case ORDA_BF16:
       rc = row_phases<__nv_bfloat16>(args, P, ws, c, s, false, true, row_stats, row_sums);

@@ -34,6 +34,7 @@ struct RowParams {
   void* ws_s; void* ws_t; int64_t ld_ws;
   const void* t_gmem; int64_t ld_tg; int32_t tg_dtype;
   int32_t* status;
+  const float* grad_scale;  // optional device scalar multiplying the dlogits (1/count for mean)
 };
 
 __device__ __forceinline__ Partial warp_merge(Partial a, double inv_t, bool cross) {
@@ -411,6 +412,7 @@ __global__ void __launch_bounds__(256) grad_sweep_kernel(RowParams p) {
       rrev = r[RS_CROSS] / r[RS_SUMT_S] - c.log_st - c.ms * it + c.log_tt + c.mt * it;
     }
     if (DK == DK_JSD) gsum = p.row_sums[row * 2 + 1];
+    const float gscale = p.grad_scale ? *p.grad_scale : 1.f;
     WsT* rs = static_cast<WsT*>(p.ws_s) + row * p.ld_ws;
     WsT* rt = static_cast<WsT*>(p.ws_t) + row * p.ld_ws;
     for (int64_t j0 = (int64_t)lane * 8; j0 < p.vocab; j0 += 256) {
@@ -449,10 +451,10 @@ __global__ void __launch_bounds__(256) grad_sweep_kernel(RowParams p) {
             }
             g += kls * d;
           }
-          gs[j] = g;
+          gs[j] = g * gscale;
           if (TSRC != TS_NONE && grad_t) {
             if (!have_pt1) pt1 = __expf(dt[j] - c.log_t1);
-            gt[j] = p.w_t * (pt1 - onehot);
+            gt[j] = p.w_t * (pt1 - onehot) * gscale;
           } else {
             gt[j] = 0.f;
           }
@@ -540,6 +542,41 @@ __global__ void finalize_kernel(const float* row_losses, int64_t ld, const int64
     out[ORDA_OUT_SUM_KL] = (float)s[2];
     out[ORDA_OUT_COUNT] = (float)s[3];
   }
+}
+
+// out[ORDA_OUT_MEAN_SCALE] before any gradient is formed: 1/max(count of non-ignored labels, 1) for
+// mean reduction, 1 for sum (tied_teacher.py:503-513). Single block.
+__global__ void mean_scale_kernel(const int64_t* labels, int64_t n, int64_t ignore_index, int32_t reduction,
+                                  float* out) {
+  __shared__ int64_t red[32];
+  int64_t c = 0;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) c += labels[i] != ignore_index;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) c += __shfl_down_sync(0xffffffffu, c, off);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = c;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int64_t t = 0;
+    for (int i = 0; i < (int)(blockDim.x / 32); ++i) t += red[i];
+    out[ORDA_OUT_MEAN_SCALE] = reduction == ORDA_REDUCTION_MEAN ? 1.f / (float)(t > 1 ? t : 1) : 1.f;
+  }
+}
+
+// data *= *scale in place; every block returns at once when *scale == 1 (no memory traffic).
+template <typename T>
+__global__ void scale_grad_kernel(T* data, int64_t n, const float* scale) {
+  const float s = *scale;
+  if (s == 1.f) return;
+  const int64_t n8 = n / 8;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    float v[8];
+    load8<T>(data + 8 * i, v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] *= s;
+    store8<T>(data + 8 * i, v);
+  }
+  for (int64_t i = 8 * n8 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    data[i] = Conv<T>::from_f(Conv<T>::to_f(data[i]) * s);
 }
 
 }  // namespace orda

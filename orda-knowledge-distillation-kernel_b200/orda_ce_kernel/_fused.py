@@ -206,12 +206,40 @@ def prepare_call(student_hidden, teacher_hidden, weight, teacher_weight, labels,
     a.grad_teacher_hidden, a.grad_teacher_weight = _ptr(g_ht), _ptr(g_wt)
     a.grad_weight_fp32 = int(f32_acc)
     a.device_status = _ptr(status)
+    a.grads_include_mean_scale = 1  # dlogits carry 1/count: backward only multiplies by grad_output
 
     pr = Prepared()
     pr.args, pr.keep = a, (hs_c, w_c, ht_c, wt_c, tl_c, labels_c)
     pr.g_hs, pr.g_ht, pr.g_w, pr.g_wt = g_hs, g_ht, g_w, g_wt
     pr.out, pr.status, pr.h, pr.h_t, pr.dev = out, status, h, h_t, dev
     return pr
+
+
+def rescale_saved_grads(ctx, grads, grad_output):
+    """Backward of the fused Functions: the stored gradients already include the mean scale, so each
+    is multiplied by ``grad_output`` - in place on the device (a no-op when grad_output == 1, the
+    usual ``loss.backward()``), or out of place where the stored buffer is padded or in another dtype.
+    Repeated backward calls (retain_graph) divide out the factor already applied."""
+    lib = _native.load()
+    go = grad_output.detach().to(torch.float32).reshape(()).contiguous()
+    if not hasattr(ctx, "applied"):
+        ctx.applied = [None] * len(grads)
+    stream = torch.cuda.current_stream(go.device).cuda_stream
+    out = []
+    for i, (g, cols, dtype) in enumerate(grads):
+        if g is None:
+            out.append(None)
+            continue
+        if ctx.applied[i] is not None:
+            out.append((g[:, :cols] * (go / ctx.applied[i])).to(dtype))
+        elif g.shape[1] == cols and g.dtype == dtype and g.is_contiguous():
+            _native.check(lib.orda_scale_grad(g.data_ptr(), g.numel(), _DTYPE_CODE[g.dtype], go.data_ptr(), stream),
+                          "orda_scale_grad")
+            ctx.applied[i] = go.clone()
+            out.append(g)
+        else:
+            out.append((g[:, :cols] * go).to(dtype))
+    return out
 
 
 class FusedDistillFunction(torch.autograd.Function):
@@ -263,29 +291,14 @@ class FusedDistillFunction(torch.autograd.Function):
     @staticmethod
     @once_differentiable
     def backward(ctx, grad_output, _g1=None, _g2=None, _g3=None):
-        g_hs, g_ht, g_w, g_wt, mean_scale, _status = ctx.saved_tensors
+        g_hs, g_ht, g_w, g_wt, _mean_scale, _status = ctx.saved_tensors
         if grad_output is None:
             return (None,) * 7
         h, h_t = ctx.shapes
         dt_hs, dt_ht, dt_w, dt_wt = ctx.dtypes
-        eff = grad_output.to(torch.float32) * mean_scale
-
-        def scale(g, cols, dtype):
-            if g is None:
-                return None
-            if g.shape[1] != cols:
-                g = g[:, :cols]
-            return (g * eff).to(dtype)
-
-        return (
-            scale(g_hs, h, dt_hs),
-            scale(g_ht, h_t, dt_ht),
-            scale(g_w, h, dt_w),
-            scale(g_wt, h_t, dt_wt),
-            None,
-            None,
-            None,
-        )
+        r = rescale_saved_grads(ctx, [(g_hs, h, dt_hs), (g_ht, h_t, dt_ht), (g_w, h, dt_w), (g_wt, h_t, dt_wt)],
+                                grad_output)
+        return (r[0], r[1], r[2], r[3], None, None, None)
 
 
 def fused_distillation(

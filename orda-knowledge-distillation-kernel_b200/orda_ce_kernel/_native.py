@@ -73,7 +73,7 @@ class DistillArgs(ctypes.Structure):
         ("phase_events", _vp),
         ("dweight_done_event", _vp),
         ("dweight_first", _i32),
-        ("reserved0", _i32),
+        ("grads_include_mean_scale", _i32),
     ]
 
 
@@ -86,6 +86,7 @@ EXPORTED_SYMBOLS = (
     "orda_distill_workspace_bytes",
     "orda_distill_fwdbwd",
     "orda_distill_fwdbwd_static_ws",
+    "orda_scale_grad",
     "orda_shard_workspace_bytes",
     "orda_shard_forward",
     "orda_merge_row_stats",
@@ -114,6 +115,8 @@ def _declare(lib):
     lib.orda_distill_workspace_bytes.argtypes = [P]
     lib.orda_distill_fwdbwd.restype = _i32
     lib.orda_distill_fwdbwd.argtypes = [P, _vp, ctypes.c_size_t, _vp]
+    lib.orda_scale_grad.restype = _i32
+    lib.orda_scale_grad.argtypes = [_vp, _i64, _i32, _vp, _vp]
     lib.orda_distill_fwdbwd_static_ws.restype = _i32
     lib.orda_distill_fwdbwd_static_ws.argtypes = [P, _vp]
     lib.orda_shard_workspace_bytes.restype = ctypes.c_size_t

@@ -24,7 +24,7 @@ import torch.distributed as dist
 from torch.autograd.function import once_differentiable
 
 from . import _native
-from ._fused import FusedSpec, prepare_call
+from ._fused import FusedSpec, prepare_call, rescale_saved_grads
 from .api import (
     DistillationLossOutput,
     PrecomputedTeacher,
@@ -141,22 +141,14 @@ class _VocabShardFunction(torch.autograd.Function):
     @staticmethod
     @once_differentiable
     def backward(ctx, grad_output, *_):
-        g_hs, g_ht, g_w, g_wt, mean_scale = ctx.saved_tensors
+        g_hs, g_ht, g_w, g_wt, _mean_scale = ctx.saved_tensors
         if grad_output is None:
             return (None,) * 10
         h, h_t = ctx.shapes
         dt_hs, dt_ht, dt_w, dt_wt = ctx.dtypes
-        eff = grad_output.to(torch.float32) * mean_scale
-
-        def scale(g, cols, dtype):
-            if g is None:
-                return None
-            if g.shape[1] != cols:
-                g = g[:, :cols]
-            return (g * eff).to(dtype)
-
-        return (scale(g_hs, h, dt_hs), scale(g_ht, h_t, dt_ht), scale(g_w, h, dt_w), scale(g_wt, h_t, dt_wt),
-                None, None, None, None, None, None)
+        r = rescale_saved_grads(ctx, [(g_hs, h, dt_hs), (g_ht, h_t, dt_ht), (g_w, h, dt_w), (g_wt, h_t, dt_wt)],
+                                grad_output)
+        return (r[0], r[1], r[2], r[3], None, None, None, None, None, None)
 
 
 def vocab_parallel_distillation_loss(student_hidden, weight_shard, labels, teacher, *, vocab_offset: int,

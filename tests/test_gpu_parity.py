@@ -409,3 +409,20 @@ def test_config3_llama_shape_slice(div):
     _close(out.kl, ref.kl, atol=0.0, rtol=1e-3, name="kl")
     assert _rel_err(hs.grad, ref.d_student_hidden) < 2e-2
     assert _rel_err(w.grad, ref.d_weight) < 2e-2
+
+
+def test_backward_scales_by_grad_output_and_supports_retain_graph():
+    """Gradients are stored with the mean scale folded in; backward multiplies by grad_output in
+    place (a no-op for 1.0) and a second backward through the same graph still returns d(loss)."""
+    hs, weight, labels, teacher, tce, kw = _llm_inputs("tied", seed=71, BT=200, V=1500)
+    out = distillation_loss(hs, weight, labels, teacher, kl_weight=0.5)
+    ref = _oracle(hs, weight, labels, kw, kl_weight=0.5)
+    (out.loss * 3.0).backward(retain_graph=True)
+    assert _rel_err(hs.grad, 3.0 * ref.d_student_hidden) < 2e-2
+    assert _rel_err(weight.grad, 3.0 * ref.d_weight) < 2e-2
+    g_hs, g_w = hs.grad.clone(), weight.grad.clone()
+    hs.grad = weight.grad = None
+    out.loss.backward()
+    assert _rel_err(hs.grad, ref.d_student_hidden) < 2e-2
+    torch.testing.assert_close(hs.grad.float() * 3.0, g_hs.float(), rtol=2e-2, atol=1e-6)
+    torch.testing.assert_close(weight.grad.float() * 3.0, g_w.float(), rtol=2e-2, atol=1e-6)
