@@ -103,9 +103,6 @@ struct Plan {
   // layout
   int64_t C, n_vtiles, vpad;
   size_t off_row_losses, off_tile_stats, off_label, off_row_stats, off_row_sums, off_ws_s, off_ws_t, total;
-  // two-stream pipeline: chunks alternate between two workspace slots (slot 1 = slot 0 + slot_bytes)
-  bool overlap;
-  size_t slot_bytes;
 };
 
 int check_args(const orda_distill_args_t* a) {
@@ -185,24 +182,7 @@ Plan make_plan(const orda_distill_args_t* a, int64_t chunk_override) {
   p.off_ws_s = off; if (need_s) off = align256(off + es * p.C * p.vpad);
   p.off_ws_t = off; if (need_t) off = align256(off + es * p.C * p.vpad);
   p.total = off;
-  p.overlap = false;
-  p.slot_bytes = 0;
   return p;
-}
-
-// Single-GPU plan with the two-stream pipeline: half-size chunks in two alternating workspace slots
-// (same logits-buffer budget), so the memory-bound row pass of one chunk runs alongside the tensor-
-// bound logits GEMM of the next on the same SMs.
-Plan make_call_plan(const orda_distill_args_t* a) {
-  Plan p = make_plan(a, 0);
-  if (a->compute_dtype == ORDA_F32 || a->chunk_rows > 0 || a->n_rows < 1024) return p;
-  const int64_t half = ((a->n_rows + 1) / 2 + kTileRows - 1) / kTileRows * kTileRows;
-  const int64_t c = std::min<int64_t>(half, std::max<int64_t>(kTileRows, p.C / 2 / kTileRows * kTileRows));
-  Plan q = make_plan(a, c);
-  q.overlap = true;
-  q.slot_bytes = q.total - q.off_tile_stats;
-  q.total += q.slot_bytes;
-  return q;
 }
 
 template <typename Kernel>
@@ -249,7 +229,6 @@ struct ChunkPtrs {
   int64_t r0, rows;
   uint8_t* grad_hs; uint8_t* grad_ht;
   const uint8_t* tg;
-  float* row_losses_base;  // per-row loss buffer when it lives outside this chunk's workspace slot
 };
 
 RowParams row_params(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const ChunkPtrs& c) {
@@ -267,8 +246,7 @@ RowParams row_params(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, c
   r.label_logits = reinterpret_cast<float*>(ws + P.off_label);
   r.row_stats = reinterpret_cast<float*>(ws + P.off_row_stats);
   r.row_sums = reinterpret_cast<float*>(ws + P.off_row_sums);
-  float* rl = c.row_losses_base ? c.row_losses_base
-             : a->out_row_losses ? a->out_row_losses : reinterpret_cast<float*>(ws + P.off_row_losses);
+  float* rl = a->out_row_losses ? a->out_row_losses : reinterpret_cast<float*>(ws + P.off_row_losses);
   r.row_losses = rl + c.r0;
   r.ld_row_losses = a->n_rows;
   r.ws_s = ws + P.off_ws_s; r.ws_t = ws + P.off_ws_t; r.ld_ws = P.vpad;
@@ -546,77 +524,12 @@ int check_operands(const orda_distill_args_t* a, const Plan& P) {
   return ORDA_OK;
 }
 
-// Per-host-thread, per-device auxiliary stream and ordering events of the two-stream pipeline.
-struct PipeRes {
-  cudaStream_t aux = nullptr;
-  cudaEvent_t in = nullptr, fwd = nullptr, end = nullptr;
-};
-
-int pipe_resources(PipeRes** out) {
-  thread_local PipeRes res[64];
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ORDA_ERR_NO_DEVICE;
-  PipeRes& r = res[dev];
-  if (!r.aux) {
-    if (cudaStreamCreateWithFlags(&r.aux, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaEventCreateWithFlags(&r.in, cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&r.fwd, cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&r.end, cudaEventDisableTiming) != cudaSuccess)
-      return ORDA_ERR_CUDA;
-  }
-  *out = &r;
-  return ORDA_OK;
-}
-
-// Chunk k runs on stream k%2 with workspace slot k%2. Its logits GEMM starts after chunk k-1's logits
-// GEMM (the row pass of k-1 then overlaps it), its dW GEMM after chunk k-1's dW (accumulation order),
-// and the slot is reused only after chunk k-2 finished (same stream).
-template <typename WsT>
-int run_overlapped(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, cudaStream_t s) {
-  PipeRes* pr = nullptr;
-  int rc;
-  if ((rc = pipe_resources(&pr))) return rc;
-  cudaStream_t st[2] = {s, pr->aux};
-  float* rl = a->out_row_losses ? a->out_row_losses : reinterpret_cast<float*>(ws + P.off_row_losses);
-  cudaEventRecord(pr->in, s);
-  cudaStreamWaitEvent(pr->aux, pr->in, 0);
-  int k = 0;
-  for (int64_t r0 = 0; r0 < a->n_rows; r0 += P.C, ++k) {
-    const int64_t rows = std::min<int64_t>(P.C, a->n_rows - r0);
-    ChunkPtrs c = chunk_ptrs(a, r0, rows);
-    c.row_losses_base = rl;
-    cudaStream_t cs = st[k & 1];
-    uint8_t* slot = ws + (k & 1) * P.slot_bytes;
-    const bool last = r0 + rows >= a->n_rows;
-    const PhaseMark pm{a, cs, last};
-    if (k > 0) cudaStreamWaitEvent(cs, pr->fwd, 0);
-    pm.mark(ORDA_PHASE_LOGITS, 0);
-    if ((rc = forward_tc<WsT>(a, P, slot, c, cs))) return rc;
-    pm.mark(ORDA_PHASE_LOGITS, 1);
-    cudaEventRecord(pr->fwd, cs);
-    pm.mark(ORDA_PHASE_ROWS, 0);
-    if ((rc = row_phases<WsT>(a, P, slot, c, cs, true, true, nullptr, nullptr))) return rc;
-    pm.mark(ORDA_PHASE_ROWS, 1);
-    if (k > 0) cudaStreamWaitEvent(cs, pr->end, 0);
-    if ((rc = grad_gemms<WsT>(a, P, slot, c, r0 == 0, cs, &pm, last))) return rc;
-    cudaEventRecord(pr->end, cs);
-  }
-  cudaStreamWaitEvent(s, pr->end, 0);
-  count_launch();
-  finalize_kernel<<<1, 1024, 0, s>>>(rl, a->n_rows, a->labels, a->n_rows, a->ignore_index, a->reduction, P.flags,
-                                     a->student_ce_weight, a->teacher_ce_weight, a->kl_weight, a->out_reduced);
-  return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
-}
-
 template <typename WsT>
 int run_all(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, cudaStream_t s) {
   int rc;
   if (a->grads_include_mean_scale) {
     count_launch();
     mean_scale_kernel<<<1, 1024, 0, s>>>(a->labels, a->n_rows, a->ignore_index, a->reduction, a->out_reduced);
-  }
-  if constexpr (!std::is_same<WsT, float>::value) {
-    if (P.overlap) return run_overlapped<WsT>(a, P, ws, s);
   }
   for (int64_t r0 = 0; r0 < a->n_rows; r0 += P.C) {
     const int64_t rows = std::min<int64_t>(P.C, a->n_rows - r0);
@@ -689,13 +602,13 @@ const char* orda_status_string(int32_t status) {
 
 size_t orda_distill_workspace_bytes(const orda_distill_args_t* args) {
   if (check_args(args) != ORDA_OK) return 0;
-  return make_call_plan(args).total;
+  return make_plan(args, 0).total;
 }
 
 int32_t orda_distill_fwdbwd(const orda_distill_args_t* args, void* workspace, size_t workspace_bytes, void* stream) {
   int rc = check_args(args);
   if (rc) return rc;
-  const Plan P = make_call_plan(args);
+  const Plan P = make_plan(args, 0);
   if ((rc = check_operands(args, P))) return rc;
   if (!workspace || workspace_bytes < P.total) return ORDA_ERR_WORKSPACE;
   return dispatch_all(args, P, static_cast<uint8_t*>(workspace), static_cast<cudaStream_t>(stream));

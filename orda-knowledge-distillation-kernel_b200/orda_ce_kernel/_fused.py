@@ -39,15 +39,13 @@ _HOOKS = threading.local()
 
 
 @contextlib.contextmanager
-def instrument(phase_events=None, dweight_done_event=None, dweight_first=False, serial=False):
+def instrument(phase_events=None, dweight_done_event=None, dweight_first=False):
     """Attach CUDA events to the fused calls made inside the block (benchmarks / overlap):
     ``phase_events`` - 2*PHASES ``torch.cuda.Event(enable_timing=True)`` recorded around each phase;
     ``dweight_done_event`` - recorded when the weight gradients are complete;
-    ``dweight_first`` - run the dW GEMMs before the dH GEMMs;
-    ``serial`` - one chunk over all rows on the caller's stream (no two-stream pipeline), so the
-    phase events time each kernel alone."""
+    ``dweight_first`` - run the dW GEMMs before the dH GEMMs."""
     prev = getattr(_HOOKS, "value", None)
-    _HOOKS.value = (phase_events, dweight_done_event, dweight_first, serial)
+    _HOOKS.value = (phase_events, dweight_done_event, dweight_first)
     try:
         yield
     finally:
@@ -254,9 +252,7 @@ class FusedDistillFunction(torch.autograd.Function):
 
         hooks = getattr(_HOOKS, "value", None)
         if hooks is not None:
-            ev, done, first, serial = hooks
-            if serial:
-                a.chunk_rows = a.n_rows
+            ev, done, first = hooks
             if ev is not None:
                 handles = (ctypes.c_void_p * (2 * _native.PHASES))(*[e.cuda_event for e in ev])
                 ctx._phase_handles = handles  # keep alive for the call
