@@ -13,6 +13,7 @@ from .api import (
     TiedTeacher,
     distillation_loss,
 )
+from . import _op  # noqa: F401  (registers torch.ops.orda_b200.distill_fwdbwd for torch.compile)
 
 
 def is_available() -> bool:

@@ -105,11 +105,25 @@ class Prepared:
     __slots__ = ("args", "keep", "g_hs", "g_ht", "g_w", "g_wt", "out", "status", "h", "h_t", "dev")
 
 
+def need_grad_flags(student_hidden, teacher_hidden, weight, teacher_weight, spec: FusedSpec) -> list[bool]:
+    """Which of (student hidden, teacher hidden, lm_head, teacher lm_head) receive gradients: the
+    tensors that require them and, for the teacher, only where a teacher CE term reaches them (tied
+    teacher always; separate teacher with a teacher CE weight)."""
+    tied, sep = spec.mode == "tied", spec.mode == "separate"
+    need_hs = bool(student_hidden.requires_grad)
+    need_w = bool(weight.requires_grad)
+    need_ht = bool(teacher_hidden is not None and teacher_hidden.requires_grad
+                   and (tied or (sep and spec.teacher_ce_weight > 0)))
+    need_wt = bool(sep and spec.teacher_ce_weight > 0 and teacher_weight is not None and teacher_weight.requires_grad)
+    return [need_hs, need_ht, need_w, need_wt]
+
+
 def prepare_call(student_hidden, teacher_hidden, weight, teacher_weight, labels, teacher_logits, spec: FusedSpec,
-                 vocab_offset: int = 0, vocab_total: int | None = None) -> Prepared:
+                 vocab_offset: int = 0, vocab_total: int | None = None, need: list[bool] | None = None) -> Prepared:
     """Operands in the compute dtype (the reference's rule), TMA-friendly layout, output buffers and
     the filled ``orda_distill_args_t``. ``weight`` (and a separate teacher's weight) may be a vocab
-    shard starting at ``vocab_offset`` of a ``vocab_total``-row lm_head."""
+    shard starting at ``vocab_offset`` of a ``vocab_total``-row lm_head. ``need`` overrides the
+    gradient flags (hs, ht, w, wt) that are otherwise read from ``requires_grad``."""
     mode = spec.mode
     dev = student_hidden.device
     if dev.type != "cuda":
@@ -130,10 +144,8 @@ def prepare_call(student_hidden, teacher_hidden, weight, teacher_weight, labels,
     if cdt not in _DTYPE_CODE:
         cdt = torch.float32
 
-    need_hs = bool(student_hidden.requires_grad)
-    need_w = bool(weight.requires_grad)
-    need_ht = bool(teacher_hidden is not None and teacher_hidden.requires_grad and (tied or (sep and spec.teacher_ce_weight > 0)))
-    need_wt = bool(sep and spec.teacher_ce_weight > 0 and teacher_weight is not None and teacher_weight.requires_grad)
+    need_hs, need_ht, need_w, need_wt = (
+        need if need is not None else need_grad_flags(student_hidden, teacher_hidden, weight, teacher_weight, spec))
 
     n, h = student_hidden.shape
     vocab = weight.shape[0]
@@ -242,34 +254,41 @@ def rescale_saved_grads(ctx, grads, grad_output):
     return out
 
 
+def launch_prepared(pr: Prepared, spec: FusedSpec, keep_alive=None) -> None:
+    """One ``orda_distill_fwdbwd`` call on the current stream with a workspace from the caching
+    allocator; instrumentation hooks of :func:`instrument` are attached here."""
+    lib = _native.load()
+    a, dev, status = pr.args, pr.dev, pr.status
+    hooks = getattr(_HOOKS, "value", None)
+    if hooks is not None:
+        ev, done, first = hooks
+        if ev is not None:
+            handles = (ctypes.c_void_p * (2 * _native.PHASES))(*[e.cuda_event for e in ev])
+            if keep_alive is not None:
+                keep_alive._phase_handles = handles  # the array must outlive the call
+            a.phase_events = ctypes.cast(handles, ctypes.c_void_p)
+        if done is not None:
+            a.dweight_done_event = done.cuda_event
+        a.dweight_first = int(bool(first))
+
+    ws_bytes = int(lib.orda_distill_workspace_bytes(a))
+    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    _native.check(lib.orda_distill_fwdbwd(a, ws.data_ptr(), ws_bytes, stream), "orda_distill_fwdbwd")
+
+    if spec.validate_labels:
+        code = int(status.item())
+        if code != _native.OK:
+            raise RuntimeError(f"orda_distill_fwdbwd device status: {_native.status_string(code)}")
+
+
 class FusedDistillFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, student_hidden, teacher_hidden, weight, teacher_weight, labels, teacher_logits, spec: FusedSpec):
-        lib = _native.load()
         pr = prepare_call(student_hidden, teacher_hidden, weight, teacher_weight, labels, teacher_logits, spec)
-        a, dev, out, status = pr.args, pr.dev, pr.out, pr.status
+        launch_prepared(pr, spec, keep_alive=ctx)
+        out, status = pr.out, pr.status
         g_hs, g_ht, g_w, g_wt, h_t = pr.g_hs, pr.g_ht, pr.g_w, pr.g_wt, pr.h_t
-
-        hooks = getattr(_HOOKS, "value", None)
-        if hooks is not None:
-            ev, done, first = hooks
-            if ev is not None:
-                handles = (ctypes.c_void_p * (2 * _native.PHASES))(*[e.cuda_event for e in ev])
-                ctx._phase_handles = handles  # keep alive for the call
-                a.phase_events = ctypes.cast(handles, ctypes.c_void_p)
-            if done is not None:
-                a.dweight_done_event = done.cuda_event
-            a.dweight_first = int(bool(first))
-
-        ws_bytes = int(lib.orda_distill_workspace_bytes(a))
-        ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
-        stream = torch.cuda.current_stream(dev).cuda_stream
-        _native.check(lib.orda_distill_fwdbwd(a, ws.data_ptr(), ws_bytes, stream), "orda_distill_fwdbwd")
-
-        if spec.validate_labels:
-            code = int(status.item())
-            if code != _native.OK:
-                raise RuntimeError(f"orda_distill_fwdbwd device status: {_native.status_string(code)}")
 
         loss = out[_native.OUT_LOSS].clone()
         ce_s = out[_native.OUT_STUDENT_CE].clone()
@@ -310,4 +329,10 @@ def fused_distillation(
     teacher_logits,
     spec: FusedSpec,
 ):
+    if torch.compiler.is_compiling():
+        # inside torch.compile the call is the traceable custom op (fake implementation + autograd formula)
+        from ._op import compiled_fused_distillation
+
+        return compiled_fused_distillation(student_hidden, teacher_hidden, weight, teacher_weight, labels,
+                                           teacher_logits, spec)
     return FusedDistillFunction.apply(student_hidden, teacher_hidden, weight, teacher_weight, labels, teacher_logits, spec)

@@ -216,7 +216,6 @@ def _validate_teacher(*, mode, teacher_hidden, teacher_weight, teacher_logits, s
 
 
 # ---------------------------------------------------------------- functional API (api.py:338-437)
-@torch._dynamo.disable
 def distillation_loss(
     student_hidden: torch.Tensor,
     weight: torch.Tensor,
@@ -257,7 +256,8 @@ def distillation_loss(
             "backend='torch' (the reference's CPU formula) is not part of this build; the distillation loss "
             "runs only in the sm_100a CUDA kernels (use backend='auto' with CUDA tensors)"
         )
-    if student_hidden.device.type != "cuda" or not cuda_kernels_available():
+    # (while torch.compile traces, the library is probed when the compiled graph first runs)
+    if student_hidden.device.type != "cuda" or (not torch.compiler.is_compiling() and not cuda_kernels_available()):
         raise RuntimeError(
             f"backend={backend!r} requires CUDA tensors on a B200 (sm_100a) GPU and the built CUDA library; "
             "there is no CPU fallback"

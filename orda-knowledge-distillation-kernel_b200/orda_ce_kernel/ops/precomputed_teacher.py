@@ -15,7 +15,6 @@ from ..utils.resolver import DEFAULT_MAX_FUSED_SIZE
 from ._common import check_bt, check_labels_host, check_scalars, chunk_rows, require_kernels
 
 
-@torch._dynamo.disable
 def precomputed_distillation_loss(
     student_hidden: torch.Tensor,
     weight: torch.Tensor,

@@ -14,7 +14,6 @@ from ..utils.resolver import DEFAULT_MAX_FUSED_SIZE
 from ._common import check_bt, check_labels_host, check_scalars, chunk_rows, require_kernels
 
 
-@torch._dynamo.disable
 def tied_distillation_loss(
     student_hidden: torch.Tensor,
     teacher_hidden: torch.Tensor | None,

@@ -37,7 +37,6 @@ def _resolve_kernel_fn(teacher_mode: str):
     raise ValueError(f"teacher_mode must be 'tied', 'separate', or 'precomputed', got {teacher_mode!r}")
 
 
-@torch._dynamo.disable
 def dynamic_chunk(
     student_hidden: torch.Tensor,
     teacher_hidden: torch.Tensor | None,
