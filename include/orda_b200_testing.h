@@ -24,6 +24,19 @@ int32_t orda_debug_gemm_pair(int32_t dtype, int32_t a_mn, int32_t b_mn, const vo
                              int64_t ldb, int64_t M, int64_t N, int64_t K, float* out, int64_t ldo, int32_t* status,
                              void* stream);
 
+/* Same contract, computed by the wide CTA-pair kernel with 512 x 256 tiles (two accumulators). */
+int32_t orda_debug_gemm_wide(int32_t dtype, int32_t a_mn, int32_t b_mn, const void* A, int64_t lda, const void* B,
+                             int64_t ldb, int64_t M, int64_t N, int64_t K, float* out, int64_t ldo, int32_t* status,
+                             void* stream);
+
+/* Pipeline counters of the CTA-pair GEMMs, collected while the environment variable
+ * ORDA_GEMM_PROFILE=1 was set when the library first launched one: out[slot*8 + i] for slot 0 logits
+ * GEMM, 1 dHidden, 2 dW, 3 unused; i = 0 MMA issuer waiting for a free accumulator, 1 MMA issuer
+ * waiting for a loaded stage, 2 MMA issuer total, 3 epilogue waiting for an accumulator, 4 epilogue
+ * working, 5 producer waiting for a free stage, 6 producer total (SM clock cycles summed over CTAs),
+ * 7 tiles. Synchronous; `reset` != 0 zeroes the counters afterwards. */
+int32_t orda_debug_gemm_profile(uint64_t* out, int32_t reset);
+
 #ifdef __cplusplus
 }
 #endif

@@ -62,6 +62,17 @@ template <> struct Conv<__half> {
   static __device__ __forceinline__ __half from_f(float x) { return __float2half_rn(x); }
 };
 
+// Two floats rounded to the 16-bit type in one conversion, low half = a (memory order a, b).
+template <typename T> __device__ __forceinline__ uint32_t pack2(float a, float b);
+template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+template <> __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  const __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
 __device__ __forceinline__ float fast_exp(float x) { return __expf(x); }
 
 // Label semantics of the reference row kernels (ops/tied_teacher.py:42-44): ignore_index rows are

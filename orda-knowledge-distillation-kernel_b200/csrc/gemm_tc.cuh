@@ -43,9 +43,11 @@ struct StoreEpiParams {
 
 struct TcGemmParams {
   CUtensorMap a0, b0, a1, b1;
+  CUtensorMap ws_s_map, ws_t_map;  // wide kernel: TMA stores of the shifted logits [rows, ld_ws], 64 x 32 boxes
   int32_t m_tiles, n_tiles;
   int32_t kb0, kb1;  // k blocks of segment 0 / 1
   int32_t group_m;
+  int32_t prof_slot;  // >= 0: accumulate pipeline wait counters into g_tc2_prof[prof_slot] (testing hook)
   int32_t* status;
   FwdEpiParams fwd;
   StoreEpiParams st;

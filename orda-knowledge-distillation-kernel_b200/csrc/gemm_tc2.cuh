@@ -1,17 +1,18 @@
-// Persistent warp-specialised tcgen05 GEMM on CTA pairs (cta_group::2), 256 x 256 tiles.
+// Persistent warp-specialised tcgen05 GEMM on CTA pairs (cta_group::2), 256 x 256 tiles, storing D.
 //
 // A pair of CTAs (a 2-CTA cluster) computes one 256-row x 256-column tile: each CTA loads its own
 // 128 A rows and its own half (128 rows or columns) of the B tile, the leader CTA issues
 // tcgen05.mma.cta_group::2 (M=256, N=256) and both CTAs receive a 128 x 256 fp32 accumulator in
-// their own TMEM. Per SM this halves the B operand traffic of the 1-CTA kernel, which is what limits
-// the 1-CTA tensor pipe (most of all for MN-major operands). Every CTA loads only the tiles it
-// consumes (no multicast).
+// their own TMEM. Two accumulator buffers (512 TMEM columns) let the epilogue of one tile overlap
+// the mainloop of the next. Every CTA loads only the tiles it consumes (no multicast).
+// Used for dHidden (few output tiles: 256 x 256 tiles fill more SMs than the 512 x 256 tiles of the
+// wide kernel in gemm_tc2w.cuh) and for the testing GEMM.
 //
 //   warp 0 (each CTA) : TMA producer; transaction bytes of both CTAs land on the leader's barrier
-//   warp 1 (leader)   : MMA issuer; commits release the smem stage and signal TMEM in both CTAs
+//   warp 1 (leader)   : MMA issuer; one multicast commit releases the smem stage in both CTAs
 //   warps 2..5        : epilogue of the CTA's own 128 accumulator rows
 //
-// A modes:
+// A modes (the wide kernel uses the same names):
 //   A_PLAIN      : 128 consecutive rows of A0 per CTA (a pair covers 256 rows)
 //   A_INTERLEAVE : tied teacher - TMEM lanes 0..63 hold 64 student rows (A0) and lanes 64..127 the
 //                  SAME 64 rows of the teacher (A1); one lm_head stream feeds both distributions.
@@ -30,6 +31,15 @@ enum AMode { A_PLAIN = 0, A_INTERLEAVE = 1 };
 constexpr int kPairBN = 256;                           // tile columns of a pair
 constexpr uint32_t kPairStageBytes = 2 * kATileBytes;  // per CTA: A 128x64 + B-half 128x64
 
+// Pipeline counters of the pair kernel (testing hook, enabled per launch by prof_slot >= 0), in SM
+// clock cycles summed over CTAs: [0] MMA issuer waiting for a free accumulator, [1] MMA issuer waiting
+// for a loaded stage, [2] MMA issuer total, [3] epilogue waiting for a finished accumulator,
+// [4] epilogue working, [5] producer waiting for a free stage, [6] producer total, [7] tiles.
+constexpr int kProfSlots = 4;
+__device__ unsigned long long g_tc2_prof[kProfSlots][8];
+
+__device__ __forceinline__ long long clk() { return clock64(); }
+
 template <int AMODE>
 struct PairShape {
   static constexpr int kStages = 6;
@@ -38,63 +48,10 @@ struct PairShape {
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
-// Interleaved tied-teacher epilogue. Warps of TMEM quarters 0/1 own student rows, 2/3 the teacher
-// rows of the same 64 original rows; every thread handles its own row (tile maxima, shifted logits,
-// label logit), so the two distributions need no exchange here.
-template <typename WsT>
-__device__ __forceinline__ void fwd_interleaved_stats(const FwdEpiParams& p, uint32_t tbase, int quarter, int lane,
-                                                      int64_t row0, int64_t n0) {
-  const bool student = quarter < 2;
-  const int64_t row = row0 + (quarter & 1) * 32 + lane;
-  const bool row_ok = row < p.rows;
-  const uint32_t f = p.flags;
-  const bool write_ws = row_ok && (student ? (f & F_WRITE_WS_S) != 0 : (f & F_WRITE_WS_T) != 0);
-  WsT* ws = static_cast<WsT*>(student ? p.ws_s : p.ws_t) + row * p.ld_ws;
-  int64_t label_local = -1;
-  if (row_ok) {
-    bool ignored;
-    const int64_t ys = safe_label(p.labels[row], p.ignore_index, p.vocab_total, &ignored);
-    if (!ignored) label_local = ys - p.vocab_offset;
-  }
-#pragma unroll 1
-  for (int h = 0; h < 2; ++h) {
-    const int64_t nh = n0 + h * kVocabTile;
-    const int tile = static_cast<int>(nh / kVocabTile);
-    if (tile >= p.n_vtiles) break;  // warp-uniform
-    const int nvalid = static_cast<int>(p.vocab - nh < kVocabTile ? p.vocab - nh : kVocabTile);
-    const int label_col = (label_local >= nh && label_local < nh + nvalid) ? static_cast<int>(label_local - nh) : -1;
-    const uint32_t tb = tbase + static_cast<uint32_t>(h * kVocabTile);
-    float m = -CUDART_INF_F;
-#pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-      float v[32];
-      tmem_ld32(tb + c * 32, v);
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (c * 32 + j < nvalid) m = fmaxf(m, v[j]);
-    }
-    float zy = 0.f;
-#pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-      float v[32];
-      tmem_ld32(tb + c * 32, v);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        if (c * 32 + j == label_col) zy = v[j];
-        v[j] -= m;
-      }
-      if (write_ws) store_chunk32<WsT>(ws + nh + c * 32, v);
-    }
-    if (row_ok) {
-      p.tile_stats[(row * p.n_vtiles + tile) * kTileStats + (student ? TS_MAX_S : TS_MAX_T)] = m;
-      if (label_col >= 0) p.label_logits[row * 2 + (student ? 0 : 1)] = zy;
-    }
-  }
-}
-
 template <bool A_MN, bool B_MN, int AMODE, bool TWO_SEG, int EPI, typename T16>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     tc2_gemm_kernel(const __grid_constant__ TcGemmParams p) {
+  static_assert(EPI == EPI_STORE, "the 256 x 256 pair kernel stores D; the logits epilogue runs in the wide kernel");
   using S = PairShape<AMODE>;
   constexpr uint32_t kIdesc = make_idesc_f16(std::is_same<T16, __nv_bfloat16>::value ? 1u : 0u, 256, kPairBN,
                                              A_MN ? 1u : 0u, B_MN ? 1u : 0u);
@@ -150,12 +107,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      const bool prof = p.prof_slot >= 0;
+      long long w_empty = 0, t_start = prof ? clk() : 0;
       for (int32_t t = pair; t < num_tiles && ok; t += npairs) {
         int32_t mt, nt;
         tile_coords(t, p.m_tiles, p.n_tiles, p.group_m, mt, nt);
         const int32_t n_cta = nt * kPairBN + static_cast<int32_t>(rank) * 128;
         for (int32_t kb = 0; kb < kb_total; ++kb) {
+          const long long c0 = prof ? clk() : 0;
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.status)) { ok = false; break; }
+          if (prof) w_empty += clk() - c0;
           const uint32_t sa = tiles_addr + stage * kPairStageBytes;
           const uint32_t sb = sa + kATileBytes;
           const uint32_t lead_full = map_to_cta(full_bar(stage), 0);
@@ -186,6 +147,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
           if (++stage == S::kStages) { stage = 0; phase ^= 1u; }
         }
       }
+      if (prof) {
+        atomicAdd(&g_tc2_prof[p.prof_slot][5], static_cast<unsigned long long>(w_empty));
+        atomicAdd(&g_tc2_prof[p.prof_slot][6], static_cast<unsigned long long>(clk() - t_start));
+      }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader CTA only)
@@ -194,22 +159,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
+      const bool prof = p.prof_slot >= 0;
+      long long w_acc = 0, w_full = 0, t_start = prof ? clk() : 0;
       for (int32_t t = pair; t < num_tiles && ok; t += npairs, ++it) {
         const int buf = it & 1;
         const uint32_t bphase = (it >> 1) & 1;
+        long long c0 = prof ? clk() : 0;
         if (!mbar_wait_cluster(tempty_bar(buf), bphase ^ 1u, p.status)) { ok = false; break; }
+        if (prof) w_acc += clk() - c0;
         tc_fence_after();
         const uint32_t acc = tmem_base + buf * kPairBN;
         for (int32_t kb = 0; kb < kb_total; ++kb) {
-          if (!mbar_wait_cluster(full_bar(stage), phase, p.status)) { ok = false; break; }
+          if (prof) c0 = clk();
+          // the stage's bytes of both CTAs complete on this CTA's barrier: a CTA-scope wait suffices
+          if (!mbar_wait(full_bar(stage), phase, p.status)) { ok = false; break; }
+          if (prof) w_full += clk() - c0;
           tc_fence_after();
           const uint32_t sa = tiles_addr + stage * kPairStageBytes;
           const uint32_t sb = sa + kATileBytes;
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)
             tc_mma_f16_pair(acc, operand_desc<A_MN>(sa, kk), operand_desc<B_MN>(sb, kk), kIdesc, (kb | kk) != 0);
-          tc_commit_pair(map_to_cta(empty_bar(stage), 0));
-          tc_commit_pair(map_to_cta(empty_bar(stage), 1));
+          tc_commit_pair_mc(empty_bar(stage), 3);  // frees the stage in both CTAs with one commit
           if (++stage == S::kStages) { stage = 0; phase ^= 1u; }
         }
         if (ok) {
@@ -217,47 +188,45 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
           tc_commit_pair(map_to_cta(tfull_bar(buf), 1));
         }
       }
+      if (prof) {
+        atomicAdd(&g_tc2_prof[p.prof_slot][0], static_cast<unsigned long long>(w_acc));
+        atomicAdd(&g_tc2_prof[p.prof_slot][1], static_cast<unsigned long long>(w_full));
+        atomicAdd(&g_tc2_prof[p.prof_slot][2], static_cast<unsigned long long>(clk() - t_start));
+        atomicAdd(&g_tc2_prof[p.prof_slot][7], static_cast<unsigned long long>(it));
+      }
     }
   } else {
     // ------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     int it = 0;
+    const bool prof = p.prof_slot >= 0 && warp == 2 && lane == 0;
+    long long w_tfull = 0, busy = 0;
     for (int32_t t = pair; t < num_tiles; t += npairs, ++it) {
       const int buf = it & 1;
       const uint32_t bphase = (it >> 1) & 1;
+      const long long c0 = prof ? clk() : 0;
       if (!mbar_wait(tfull_bar(buf), bphase, p.status)) break;
+      const long long c1 = prof ? clk() : 0;
+      if (prof) w_tfull += c1 - c0;
       tc_fence_after();
       int32_t mt, nt;
       tile_coords(t, p.m_tiles, p.n_tiles, p.group_m, mt, nt);
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * kPairBN;
       const int64_t n0 = static_cast<int64_t>(nt) * kPairBN;
-      if constexpr (EPI == EPI_FWD_STATS) {
-        if constexpr (AMODE == A_INTERLEAVE) {
-          const int64_t row0 = static_cast<int64_t>(mt) * 128 + rank * 64;
-          fwd_interleaved_stats<T16>(p.fwd, tbase, quarter, lane, row0, n0);
-        } else {
-          const int64_t row = static_cast<int64_t>(mt) * 256 + rank * 128 + r;
-#pragma unroll 1
-          for (int h = 0; h < 2; ++h) {
-            const int64_t nh = n0 + h * kVocabTile;
-            const int tile = static_cast<int>(nh / kVocabTile);
-            if (tile < p.fwd.n_vtiles) {  // warp-uniform
-              TmemSrc<0> src{tbase + static_cast<uint32_t>(h * kVocabTile)};
-              fwd_tile_stats<T16, false>(p.fwd, row, row < p.fwd.rows, nh, tile, src);
-            }
-          }
-        }
-      } else {
-        const int64_t row = static_cast<int64_t>(mt) * 256 + rank * 128 + r;
-        store_epilogue<T16>(p.st, tbase, row, n0, kPairBN);
-      }
+      const int64_t row = static_cast<int64_t>(mt) * 256 + rank * 128 + r;
+      store_epilogue<T16>(p.st, tbase, row, n0, kPairBN);
       tc_fence_before();
       __syncwarp();
+      if (prof) busy += clk() - c1;
       if (lane == 0) {
         if (rank == 0) mbar_arrive(tempty_bar(buf));
         else mbar_arrive_cluster(map_to_cta(tempty_bar(buf), 0));
       }
+    }
+    if (prof) {
+      atomicAdd(&g_tc2_prof[p.prof_slot][3], static_cast<unsigned long long>(w_tfull));
+      atomicAdd(&g_tc2_prof[p.prof_slot][4], static_cast<unsigned long long>(busy));
     }
   }
 

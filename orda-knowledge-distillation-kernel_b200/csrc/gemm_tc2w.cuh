@@ -1,0 +1,399 @@
+// Persistent warp-specialised tcgen05 GEMM on CTA pairs with 512 x 256 tiles ("wide" pair kernel).
+//
+// Each tile issues two M=256 pair MMAs per k step (tcgen05.mma.cta_group::2, N=256) into two
+// accumulators that fill all 512 TMEM columns of each CTA. Per CTA and 64-deep k block the kernel
+// loads 256 A rows and its 128-column half of B (48 KB) for 2 x 128 x 256 x 64 multiply-adds: two
+// thirds of the operand bytes per MMA of the 256 x 256 pair kernel. That ratio is what keeps the
+// tensor pipe fed from L2: the 256 x 256 kernel leaves the MMA issuer waiting for loaded stages
+// about 16% of the time.
+//
+// The accumulators are single-buffered. The epilogue drains accumulator 0 and then accumulator 1,
+// releasing each as soon as it is read, and the MMA issuer of the next tile waits for each one
+// separately. The logits epilogue reads each 128-column vocab tile from TMEM with all its loads in
+// flight at once, stages the shifted logits in shared memory (128-byte swizzle) and writes them with
+// TMA stores, so the part of the epilogue that is not hidden stays short.
+//
+//   warp 0 (each CTA) : TMA producer; transaction bytes of both CTAs land on the leader's barrier
+//   warp 1 (leader)   : MMA issuer
+//   warps 2..5        : epilogue of the CTA's TMEM lanes (32 per warp)
+//
+// Row mapping of a tile (pair rows 0..511; CTA rank r, accumulator j, TMEM lane l):
+//   A_PLAIN      : row j*256 + r*128 + l
+//   A_INTERLEAVE : token j*128 + r*64 + (l & 63); lanes 0..63 student (A0), 64..127 teacher (A1)
+#pragma once
+
+#include "distill_common.cuh"
+#include "fwd_epilogue.cuh"
+#include "gemm_tc.cuh"
+#include "gemm_tc2.cuh"
+#include "sm100_ptx.cuh"
+
+namespace orda {
+
+constexpr uint32_t kWideAcc = 2;                              // accumulators per CTA (256 columns each)
+constexpr uint32_t kWideStageBytes = 2 * kATileBytes + kATileBytes;  // A: 2 x 128 rows, B: 128-column half
+constexpr uint32_t kWideStagingBytes = 4 * 8192;              // per epilogue warp: 32 rows x 128 cols, 16-bit
+
+template <int EPI>
+struct WideShape {
+  static constexpr int kStages = 4;
+  static constexpr uint32_t kStaging = EPI == EPI_FWD_STATS ? kWideStagingBytes : 0;
+  static constexpr uint32_t kBarBytes = (2 * kStages + 4) * 8 + 16;
+  static constexpr uint32_t kSmemBytes = kStages * kWideStageBytes + kStaging + kBarBytes + 1024;
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+};
+
+// Logits epilogue of one 256-column accumulator for the warp's 32 rows (one row per lane): per
+// 128-column vocab tile the tile maximum, the exact label logit and the logits shifted by the maximum
+// (16-bit, through the warp's staging buffer and a TMA store). The TMEM loads of the second vocab tile
+// are issued before the first tile's shifted logits are staged and stored, so their latency overlaps.
+template <typename WsT>
+__device__ __forceinline__ void wide_fwd_acc(const FwdEpiParams& p, const CUtensorMap* ws_map, bool write_ws,
+                                             uint32_t tbase, uint32_t staging, int64_t row, int64_t y0,
+                                             int64_t n0, bool student, int lane, int64_t label_raw) {
+  const bool row_ok = row < p.rows;
+  int64_t label_local = -1;
+  if (row_ok) {
+    bool ignored;
+    const int64_t y = safe_label(label_raw, p.ignore_index, p.vocab_total, &ignored);
+    if (!ignored) label_local = y - p.vocab_offset;
+  }
+  const int tile0 = static_cast<int>(n0 / kVocabTile);
+  const int ntiles = p.n_vtiles - tile0 < 2 ? p.n_vtiles - tile0 : 2;  // warp-uniform, >= 1
+  uint32_t r[4][32];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) tmem_ld32_async(tbase + c * 32, r[c]);
+#pragma unroll 1
+  for (int h = 0; h < ntiles; ++h) {
+    const int64_t nh = n0 + h * kVocabTile;
+    const int tile = tile0 + h;
+    const int nvalid = static_cast<int>(p.vocab - nh < kVocabTile ? p.vocab - nh : kVocabTile);
+    const int label_col = (label_local >= nh && label_local < nh + nvalid) ? static_cast<int>(label_local - nh) : -1;
+    tmem_wait_ld();
+    float m = -CUDART_INF_F;
+    if (nvalid == kVocabTile) {
+      float pm[8];  // independent partial maxima: short dependency chains
+#pragma unroll
+      for (int q = 0; q < 8; ++q) pm[q] = -CUDART_INF_F;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int j = 0; j < 32; ++j) pm[j & 7] = fmaxf(pm[j & 7], __uint_as_float(r[c][j]));
+#pragma unroll
+      for (int q = 0; q < 8; ++q) m = fmaxf(m, pm[q]);
+    } else {
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (c * 32 + j < nvalid) m = fmaxf(m, __uint_as_float(r[c][j]));
+    }
+    float zy = 0.f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      if (__any_sync(0xffffffffu, static_cast<unsigned>(label_col - c * 32) < 32u)) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (c * 32 + j == label_col) zy = __uint_as_float(r[c][j]);
+      }
+    }
+    // shifted logits packed two per register; the fp32 registers are then free for the next tile
+    uint32_t w[64];
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        w[c * 16 + e] = pack2<WsT>(__uint_as_float(r[c][2 * e]) - m, __uint_as_float(r[c][2 * e + 1]) - m);
+    if (h + 1 < ntiles) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32_async(tbase + kVocabTile + c * 32, r[c]);
+    }
+
+    if (write_ws) {
+      // the previous TMA store of this warp must have read the staging buffer
+      if (lane == 0) bulk_wait_read_all();
+      __syncwarp();
+      // row `lane` of the two 64-column halves: 16-byte chunk q of a 128-byte row lands at q ^ (lane & 7)
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        const uint32_t addr = staging + (q >> 3) * 4096u + static_cast<uint32_t>(lane) * 128u +
+                              ((static_cast<uint32_t>(q & 7) ^ static_cast<uint32_t>(lane & 7)) << 4);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w[4 * q]), "r"(w[4 * q + 1]),
+                     "r"(w[4 * q + 2]), "r"(w[4 * q + 3])
+                     : "memory");
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(ws_map, staging, static_cast<int32_t>(nh), static_cast<int32_t>(y0));
+        tma_store_2d(ws_map, staging + 4096u, static_cast<int32_t>(nh + 64), static_cast<int32_t>(y0));
+        bulk_commit_group();
+      }
+    }
+    if (row_ok) {
+      p.tile_stats[(row * p.n_vtiles + tile) * kTileStats + (student ? TS_MAX_S : TS_MAX_T)] = m;
+      if (label_col >= 0) p.label_logits[row * 2 + (student ? 0 : 1)] = zy;
+    }
+  }
+  tmem_wait_ld();  // no TMEM load of this warp stays in flight past the accumulator's release
+}
+
+template <bool A_MN, bool B_MN, int AMODE, bool TWO_SEG, int EPI, typename T16>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    tc2w_gemm_kernel(const __grid_constant__ TcGemmParams p) {
+  using S = WideShape<EPI>;
+  constexpr uint32_t kIdesc = make_idesc_f16(std::is_same<T16, __nv_bfloat16>::value ? 1u : 0u, 256, kPairBN,
+                                             A_MN ? 1u : 0u, B_MN ? 1u : 0u);
+  constexpr uint32_t kTmemCols = 512;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t tiles_addr = (raw_addr + 1023u) & ~1023u;
+  const uint32_t staging_addr = tiles_addr + S::kStages * kWideStageBytes;
+  const uint32_t bar_addr = staging_addr + S::kStaging;
+  auto full_bar = [&](int s) { return bar_addr + 8u * s; };
+  auto empty_bar = [&](int s) { return bar_addr + 8u * (S::kStages + s); };
+  const uint32_t tfull = bar_addr + 8u * (2 * S::kStages);
+  auto tempty_bar = [&](int j) { return bar_addr + 8u * (2 * S::kStages + 1 + j); };
+  const uint32_t tmem_slot = bar_addr + 8u * (2 * S::kStages + 4);
+  uint32_t* tmem_slot_ptr = reinterpret_cast<uint32_t*>(smem_raw + (tmem_slot - raw_addr));
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();
+  const int32_t pair = blockIdx.x / 2, npairs = gridDim.x / 2;
+  const int32_t num_tiles = p.m_tiles * p.n_tiles;
+  const int32_t kb_total = TWO_SEG ? p.kb0 + p.kb1 : p.kb0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::kStages; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    mbar_init(tfull, 1);
+    for (int j = 0; j < 2; ++j) mbar_init(tempty_bar(j), 8);  // one elected lane per epilogue warp of both CTAs
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&p.a0);
+    tma_prefetch_desc(&p.b0);
+    if (AMODE == A_INTERLEAVE || TWO_SEG) tma_prefetch_desc(&p.a1);
+    if (TWO_SEG) tma_prefetch_desc(&p.b1);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot_ptr;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      const bool prof = p.prof_slot >= 0;
+      long long w_empty = 0, t_start = prof ? clk() : 0;
+      for (int32_t t = pair; t < num_tiles && ok; t += npairs) {
+        int32_t mt, nt;
+        tile_coords(t, p.m_tiles, p.n_tiles, p.group_m, mt, nt);
+        const int32_t n_cta = nt * kPairBN + static_cast<int32_t>(rank) * 128;
+        for (int32_t kb = 0; kb < kb_total; ++kb) {
+          const long long c0 = prof ? clk() : 0;
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.status)) { ok = false; break; }
+          if (prof) w_empty += clk() - c0;
+          const uint32_t sa = tiles_addr + stage * kWideStageBytes;
+          const uint32_t sb = sa + 2 * kATileBytes;
+          const uint32_t lead_full = map_to_cta(full_bar(stage), 0);
+          if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), 2 * kWideStageBytes);
+          const bool seg1 = TWO_SEG && kb >= p.kb0;
+          const int32_t k0 = (seg1 ? kb - p.kb0 : kb) * kBK;
+          const CUtensorMap* amap = seg1 ? &p.a1 : &p.a0;
+          const CUtensorMap* bmap = seg1 ? &p.b1 : &p.b0;
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const uint32_t saj = sa + j * kATileBytes;
+            if constexpr (AMODE == A_INTERLEAVE) {
+              const int32_t r = mt * 256 + j * 128 + static_cast<int32_t>(rank) * 64;
+              tma_load_2d_pair(saj, &p.a0, lead_full, k0, r);
+              tma_load_2d_pair(saj + 8192u, &p.a1, lead_full, k0, r);
+            } else {
+              const int32_t m_cta = mt * 512 + j * 256 + static_cast<int32_t>(rank) * 128;
+              if constexpr (A_MN) {
+                tma_load_2d_pair(saj, amap, lead_full, m_cta, k0);
+                tma_load_2d_pair(saj + 8192u, amap, lead_full, m_cta + 64, k0);
+              } else {
+                tma_load_2d_pair(saj, amap, lead_full, k0, m_cta);
+              }
+            }
+          }
+          if constexpr (B_MN) {
+            tma_load_2d_pair(sb, bmap, lead_full, n_cta, k0);
+            tma_load_2d_pair(sb + 8192u, bmap, lead_full, n_cta + 64, k0);
+          } else {
+            tma_load_2d_pair(sb, bmap, lead_full, k0, n_cta);
+          }
+          if (++stage == S::kStages) { stage = 0; phase ^= 1u; }
+        }
+      }
+      if (prof) {
+        atomicAdd(&g_tc2_prof[p.prof_slot][5], static_cast<unsigned long long>(w_empty));
+        atomicAdd(&g_tc2_prof[p.prof_slot][6], static_cast<unsigned long long>(clk() - t_start));
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader CTA only)
+    if (rank == 0 && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      const bool prof = p.prof_slot >= 0;
+      long long w_acc = 0, w_full = 0, t_start = prof ? clk() : 0;
+      for (int32_t t = pair; t < num_tiles && ok; t += npairs, ++it) {
+        const uint32_t bphase = static_cast<uint32_t>(it & 1);
+        // Head of the tile: the first `nhead` stages feed accumulator 0 as soon as the epilogue has
+        // drained it, while the epilogue still drains accumulator 1; then the same stages feed
+        // accumulator 1. After the head both accumulators advance together stage by stage.
+        const int32_t nhead = kb_total < S::kStages ? kb_total : S::kStages;
+        const int stage0 = stage;
+        long long c0 = prof ? clk() : 0;
+        if (!mbar_wait_cluster(tempty_bar(0), bphase ^ 1u, p.status)) { ok = false; break; }
+        if (prof) w_acc += clk() - c0;
+        tc_fence_after();
+        for (int32_t kb = 0; kb < nhead; ++kb) {
+          if (prof) c0 = clk();
+          if (!mbar_wait(full_bar(stage), phase, p.status)) { ok = false; break; }
+          if (prof) w_full += clk() - c0;
+          tc_fence_after();
+          const uint32_t sa = tiles_addr + stage * kWideStageBytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            tc_mma_f16_pair(tmem_base, operand_desc<A_MN>(sa, kk), operand_desc<B_MN>(sa + 2 * kATileBytes, kk),
+                            kIdesc, (kb | kk) != 0);
+          if (++stage == S::kStages) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        if (prof) c0 = clk();
+        if (!mbar_wait_cluster(tempty_bar(1), bphase ^ 1u, p.status)) { ok = false; break; }
+        if (prof) w_acc += clk() - c0;
+        tc_fence_after();
+        for (int32_t kb = 0; kb < nhead; ++kb) {
+          const int hs = (stage0 + kb) % S::kStages;
+          const uint32_t sa = tiles_addr + hs * kWideStageBytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            tc_mma_f16_pair(tmem_base + kPairBN, operand_desc<A_MN>(sa + kATileBytes, kk),
+                            operand_desc<B_MN>(sa + 2 * kATileBytes, kk), kIdesc, (kb | kk) != 0);
+          tc_commit_pair_mc(empty_bar(hs), 3);
+        }
+        for (int32_t kb = nhead; kb < kb_total; ++kb) {
+          if (prof) c0 = clk();
+          // the stage's bytes of both CTAs complete on this CTA's barrier: a CTA-scope wait suffices
+          if (!mbar_wait(full_bar(stage), phase, p.status)) { ok = false; break; }
+          if (prof) w_full += clk() - c0;
+          tc_fence_after();
+          const uint32_t sa = tiles_addr + stage * kWideStageBytes;
+          const uint32_t sb = sa + 2 * kATileBytes;
+#pragma unroll
+          for (int jj = 0; jj < 2; ++jj)
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk)
+              tc_mma_f16_pair(tmem_base + jj * kPairBN, operand_desc<A_MN>(sa + jj * kATileBytes, kk),
+                              operand_desc<B_MN>(sb, kk), kIdesc, 1u);
+          tc_commit_pair_mc(empty_bar(stage), 3);  // frees the stage in both CTAs with one commit
+          if (++stage == S::kStages) { stage = 0; phase ^= 1u; }
+        }
+        if (ok) {
+          tc_commit_pair(map_to_cta(tfull, 0));
+          tc_commit_pair(map_to_cta(tfull, 1));
+        }
+      }
+      if (prof) {
+        atomicAdd(&g_tc2_prof[p.prof_slot][0], static_cast<unsigned long long>(w_acc));
+        atomicAdd(&g_tc2_prof[p.prof_slot][1], static_cast<unsigned long long>(w_full));
+        atomicAdd(&g_tc2_prof[p.prof_slot][2], static_cast<unsigned long long>(clk() - t_start));
+        atomicAdd(&g_tc2_prof[p.prof_slot][7], static_cast<unsigned long long>(it));
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
+    const int quarter = warp & 3;
+    const uint32_t staging = staging_addr + static_cast<uint32_t>(quarter) * 8192u;
+    int it = 0;
+    const bool prof = p.prof_slot >= 0 && warp == 2 && lane == 0;
+    long long w_tfull = 0, busy = 0;
+
+    for (int32_t t = pair; t < num_tiles; t += npairs, ++it) {
+      // labels of this lane's two rows, loaded before the wait so their latency is hidden
+      int64_t lab[2] = {0, 0};
+      if constexpr (EPI == EPI_FWD_STATS) {
+        int32_t mt0, nt0;
+        tile_coords(t, p.m_tiles, p.n_tiles, p.group_m, mt0, nt0);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int64_t row = AMODE == A_INTERLEAVE
+                                  ? static_cast<int64_t>(mt0) * 256 + j * 128 + rank * 64 + (quarter & 1) * 32 + lane
+                                  : static_cast<int64_t>(mt0) * 512 + j * 256 + rank * 128 + quarter * 32 + lane;
+          if (row < p.fwd.rows) lab[j] = p.fwd.labels[row];
+        }
+      }
+      const long long c0 = prof ? clk() : 0;
+      if (!mbar_wait(tfull, static_cast<uint32_t>(it & 1), p.status)) break;
+      const long long c1 = prof ? clk() : 0;
+      if (prof) w_tfull += c1 - c0;
+      tc_fence_after();
+      int32_t mt, nt;
+      tile_coords(t, p.m_tiles, p.n_tiles, p.group_m, mt, nt);
+      const int64_t n0 = static_cast<int64_t>(nt) * kPairBN;
+#pragma unroll 1
+      for (int j = 0; j < 2; ++j) {
+        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + j * kPairBN;
+        if constexpr (EPI == EPI_FWD_STATS) {
+          if constexpr (AMODE == A_INTERLEAVE) {
+            const bool student = quarter < 2;
+            const int64_t y0 = static_cast<int64_t>(mt) * 256 + j * 128 + rank * 64 + (quarter & 1) * 32;
+            const bool write_ws = (p.fwd.flags & (student ? F_WRITE_WS_S : F_WRITE_WS_T)) != 0;
+            wide_fwd_acc<T16>(p.fwd, student ? &p.ws_s_map : &p.ws_t_map, write_ws, tbase, staging, y0 + lane, y0, n0,
+                              student, lane, j ? lab[1] : lab[0]);
+          } else {
+            const int64_t y0 = static_cast<int64_t>(mt) * 512 + j * 256 + rank * 128 + quarter * 32;
+            wide_fwd_acc<T16>(p.fwd, &p.ws_s_map, (p.fwd.flags & F_WRITE_WS_S) != 0, tbase, staging, y0 + lane, y0,
+                              n0, true, lane, j ? lab[1] : lab[0]);
+          }
+        } else {
+          const int64_t row = static_cast<int64_t>(mt) * 512 + j * 256 + rank * 128 + quarter * 32 + lane;
+          store_epilogue<T16>(p.st, tbase, row, n0, kPairBN);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (rank == 0) mbar_arrive(tempty_bar(j));
+          else mbar_arrive_cluster(map_to_cta(tempty_bar(j), 0));
+        }
+      }
+      if (prof) busy += clk() - c1;
+    }
+    if constexpr (EPI == EPI_FWD_STATS) {
+      if (lane == 0) bulk_wait_all();  // staged stores complete before the shared memory goes away
+    }
+    if (prof) {
+      atomicAdd(&g_tc2_prof[p.prof_slot][3], static_cast<unsigned long long>(w_tfull));
+      atomicAdd(&g_tc2_prof[p.prof_slot][4], static_cast<unsigned long long>(busy));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the peer's epilogue and the leader's MMAs are all done before TMEM is freed
+  if (warp == 1) {
+    tc_fence_after();
+    if (*reinterpret_cast<volatile int32_t*>(p.status) == ORDA_ERR_TIMEOUT) __nanosleep(1000000);
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace orda

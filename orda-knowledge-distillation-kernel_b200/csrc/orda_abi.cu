@@ -19,6 +19,7 @@
 
 #include "gemm_tc.cuh"
 #include "gemm_tc2.cuh"
+#include "gemm_tc2w.cuh"
 #include "orda_b200.h"
 #include "orda_b200_testing.h"
 #include "row_kernels.cuh"
@@ -79,10 +80,6 @@ int num_sms() {
   return n > 0 ? n : 148;
 }
 
-int env_group(const char* name, int dflt) {  // tuning knob for tile rasterisation
-  const char* v = getenv(name);
-  return v ? atoi(v) : dflt;
-}
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
@@ -207,6 +204,16 @@ int launch_tc(TcGemmParams& prm, int64_t M, int64_t N, cudaStream_t stream, int 
   return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
 }
 
+// Pipeline counters of the pair GEMMs are collected when ORDA_GEMM_PROFILE=1 (testing hook; read back
+// with orda_debug_gemm_profile).
+bool gemm_profiling() {
+  static const bool on = [] {
+    const char* e = getenv("ORDA_GEMM_PROFILE");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+
 template <bool A_MN, bool B_MN, int AMODE, bool TWO_SEG, int EPI, typename T16>
 int launch_tc2(TcGemmParams& prm, int64_t M_tiles, int64_t N, cudaStream_t stream, int group_m) {
   using S = PairShape<AMODE>;
@@ -218,11 +225,33 @@ int launch_tc2(TcGemmParams& prm, int64_t M_tiles, int64_t N, cudaStream_t strea
   if (tiles > INT32_MAX) return ORDA_ERR_UNSUPPORTED;
   auto k = tc2_gemm_kernel<A_MN, B_MN, AMODE, TWO_SEG, EPI, T16>;
   set_smem(k, S::kSmemBytes);
+  prm.prof_slot = gemm_profiling() ? (EPI == EPI_FWD_STATS ? 0 : (A_MN ? 2 : 1)) : -1;
   const int pairs = static_cast<int>(std::min<int64_t>(tiles, num_sms() / 2));
   count_launch();
   k<<<2 * pairs, kGemmThreads, S::kSmemBytes, stream>>>(prm);
   return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
 }
+
+
+// Wide pair kernel (512 x 256 tiles); M_tiles counts 512-row (A_PLAIN) or 256-token (A_INTERLEAVE) tiles.
+template <bool A_MN, bool B_MN, int AMODE, bool TWO_SEG, int EPI, typename T16>
+int launch_tc2w(TcGemmParams& prm, int64_t M_tiles, int64_t N, cudaStream_t stream, int group_m) {
+  using S = WideShape<EPI>;
+  prm.m_tiles = static_cast<int32_t>(M_tiles);
+  prm.n_tiles = static_cast<int32_t>(cdiv(N, kPairBN));
+  prm.group_m = group_m;
+  const int64_t tiles = (int64_t)prm.m_tiles * prm.n_tiles;
+  if (tiles <= 0) return ORDA_OK;
+  if (tiles > INT32_MAX) return ORDA_ERR_UNSUPPORTED;
+  auto k = tc2w_gemm_kernel<A_MN, B_MN, AMODE, TWO_SEG, EPI, T16>;
+  set_smem(k, S::kSmemBytes);
+  prm.prof_slot = gemm_profiling() ? (EPI == EPI_FWD_STATS ? 0 : (A_MN ? 2 : 1)) : -1;
+  const int pairs = static_cast<int>(std::min<int64_t>(tiles, num_sms() / 2));
+  count_launch();
+  k<<<2 * pairs, kGemmThreads, S::kSmemBytes, stream>>>(prm);
+  return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
+}
+
 
 struct ChunkPtrs {
   const uint8_t* hs; const uint8_t* ht; const int64_t* labels;
@@ -273,6 +302,18 @@ FwdEpiParams fwd_params(const orda_distill_args_t* a, const Plan& P, uint8_t* ws
 }
 
 // ------------------------------------------------------------------ 16-bit (tensor core) phases
+// TMA store maps of the chunk's shifted-logit buffers ([rows, Vpad], 64 x 32 boxes) for the wide kernel.
+int ws_store_maps(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const ChunkPtrs& c, TcGemmParams& prm) {
+  int rc;
+  if (P.write_ws_s &&
+      (rc = make_map(&prm.ws_s_map, a->compute_dtype, ws + P.off_ws_s, P.vpad, c.rows, P.vpad, 64, 32)))
+    return rc;
+  if (P.teacher_acc && P.write_ws_t &&
+      (rc = make_map(&prm.ws_t_map, a->compute_dtype, ws + P.off_ws_t, P.vpad, c.rows, P.vpad, 64, 32)))
+    return rc;
+  return ORDA_OK;
+}
+
 template <typename T16>
 int forward_tc(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const ChunkPtrs& c, cudaStream_t s) {
   const int dt = a->compute_dtype;
@@ -287,7 +328,8 @@ int forward_tc(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const C
     // CTA-pair kernel: 64 student rows + the same 64 teacher rows per CTA, half the lm_head tile per CTA
     if ((rc = make_operand_map(&prm.a0, dt, c.hs, false, c.rows, a->hidden, a->ld_student_hidden, 64))) return rc;
     if ((rc = make_operand_map(&prm.a1, dt, c.ht, false, c.rows, a->hidden, a->ld_teacher_hidden, 64))) return rc;
-    return launch_tc2<false, false, A_INTERLEAVE, false, EPI_FWD_STATS, T16>(prm, cdiv(c.rows, 128), a->vocab, s, env_group("ORDA_GROUP_FWD", 16));
+    if ((rc = ws_store_maps(a, P, ws, c, prm))) return rc;
+    return launch_tc2w<false, false, A_INTERLEAVE, false, EPI_FWD_STATS, T16>(prm, cdiv(c.rows, 256), a->vocab, s, 8);
   }
   if (P.teacher_acc) {
     if ((rc = make_operand_map(&prm.a1, dt, c.ht, false, c.rows, a->teacher_hidden, a->ld_teacher_hidden, kTileRows))) return rc;
@@ -295,7 +337,8 @@ int forward_tc(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const C
     prm.kb1 = static_cast<int32_t>(cdiv(a->teacher_hidden, kBK));
     return launch_tc<kVocabTile, false, false, GM_TWO_ACC, EPI_FWD_STATS, T16>(prm, c.rows, a->vocab, s, 16);
   }
-  return launch_tc2<false, false, A_PLAIN, false, EPI_FWD_STATS, T16>(prm, cdiv(c.rows, 256), a->vocab, s, 8);
+  if ((rc = ws_store_maps(a, P, ws, c, prm))) return rc;
+  return launch_tc2w<false, false, A_PLAIN, false, EPI_FWD_STATS, T16>(prm, cdiv(c.rows, 512), a->vocab, s, 4);
 }
 
 // dH[rows, N] = dZ[rows, V] * Wm[V, N]
@@ -309,7 +352,7 @@ int dh_tc(const orda_distill_args_t* a, const Plan& P, const void* dz, const voi
   if ((rc = make_operand_map(&prm.b0, a->compute_dtype, wmat, true, n, a->vocab, ldw, 128))) return rc;
   prm.kb0 = static_cast<int32_t>(cdiv(a->vocab, kBK));
   prm.st = StoreEpiParams{out, n, rows, n, 0, 0};
-  return launch_tc2<false, true, A_PLAIN, false, EPI_STORE, T16>(prm, cdiv(rows, 256), n, s, env_group("ORDA_GROUP_DH", 8));
+  return launch_tc2<false, true, A_PLAIN, false, EPI_STORE, T16>(prm, cdiv(rows, 256), n, s, 8);
 }
 
 // dW[V, N] (+)= dZ0^T H0 (+ dZ1^T H1)
@@ -329,9 +372,9 @@ int dw_tc(const orda_distill_args_t* a, const Plan& P, const void* dz0, const vo
     if ((rc = make_operand_map(&prm.a1, dt, dz1, true, a->vocab, rows, P.vpad, kTileRows))) return rc;
     if ((rc = make_operand_map(&prm.b1, dt, h1, true, n, rows, ldh1, 128))) return rc;
     prm.kb1 = prm.kb0;
-    return launch_tc2<true, true, A_PLAIN, true, EPI_STORE, T16>(prm, cdiv(a->vocab, 256), n, s, env_group("ORDA_GROUP_DW", 8));
+    return launch_tc2w<true, true, A_PLAIN, true, EPI_STORE, T16>(prm, cdiv(a->vocab, 512), n, s, 4);
   }
-  return launch_tc2<true, true, A_PLAIN, false, EPI_STORE, T16>(prm, cdiv(a->vocab, 256), n, s, env_group("ORDA_GROUP_DW", 8));
+  return launch_tc2w<true, true, A_PLAIN, false, EPI_STORE, T16>(prm, cdiv(a->vocab, 512), n, s, 4);
 }
 
 // ------------------------------------------------------------------ fp32 (SIMT) phases
@@ -810,4 +853,43 @@ extern "C" int32_t orda_distill_fwdbwd_static_ws(const orda_distill_args_t* args
   if (cudaMemsetAsync(static_cast<uint8_t*>(ws) + P.off_label, 0, P.off_row_stats - P.off_label, s) != cudaSuccess)
     return ORDA_ERR_CUDA;
   return dispatch_all(args, P, static_cast<uint8_t*>(ws), s);
+}
+
+extern "C" int32_t orda_debug_gemm_profile(uint64_t* out, int32_t reset) {
+  if (!out) return ORDA_ERR_INVALID_ARGUMENT;
+  unsigned long long host[orda::kProfSlots][8];
+  if (cudaMemcpyFromSymbol(host, orda::g_tc2_prof, sizeof(host)) != cudaSuccess) return ORDA_ERR_CUDA;
+  memcpy(out, host, sizeof(host));
+  if (reset) {
+    memset(host, 0, sizeof(host));
+    if (cudaMemcpyToSymbol(orda::g_tc2_prof, host, sizeof(host)) != cudaSuccess) return ORDA_ERR_CUDA;
+  }
+  return ORDA_OK;
+}
+
+extern "C" int32_t orda_debug_gemm_wide(int32_t dtype, int32_t a_mn, int32_t b_mn, const void* A, int64_t lda,
+                                        const void* B, int64_t ldb, int64_t M, int64_t N, int64_t K, float* out,
+                                        int64_t ldo, int32_t* status, void* stream) {
+  if (dtype != ORDA_BF16 && dtype != ORDA_F16) return ORDA_ERR_INVALID_ARGUMENT;
+  TcGemmParams prm{};
+  prm.status = status;
+  int rc;
+  if ((rc = make_operand_map(&prm.a0, dtype, A, a_mn != 0, M, K, lda, kTileRows))) return rc;
+  if ((rc = make_operand_map(&prm.b0, dtype, B, b_mn != 0, N, K, ldb, 128))) return rc;
+  prm.kb0 = static_cast<int32_t>(cdiv(K, kBK));
+  prm.st = StoreEpiParams{out, ldo, M, N, 1, 0};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t mt = cdiv(M, 512);
+#define ORDA_DBGW(T, AM, BM) return launch_tc2w<AM, BM, A_PLAIN, false, EPI_STORE, T>(prm, mt, N, s, 4)
+  if (dtype == ORDA_BF16) {
+    if (a_mn && b_mn) ORDA_DBGW(__nv_bfloat16, true, true);
+    if (a_mn) ORDA_DBGW(__nv_bfloat16, true, false);
+    if (b_mn) ORDA_DBGW(__nv_bfloat16, false, true);
+    ORDA_DBGW(__nv_bfloat16, false, false);
+  }
+  if (a_mn && b_mn) ORDA_DBGW(__half, true, true);
+  if (a_mn) ORDA_DBGW(__half, true, false);
+  if (b_mn) ORDA_DBGW(__half, false, true);
+  ORDA_DBGW(__half, false, false);
+#undef ORDA_DBGW
 }

@@ -94,6 +94,8 @@ EXPORTED_SYMBOLS = (
     "orda_shard_backward",
     "orda_debug_gemm",
     "orda_debug_gemm_pair",
+    "orda_debug_gemm_profile",
+    "orda_debug_gemm_wide",
 )
 
 _lib = None
@@ -133,6 +135,10 @@ def _declare(lib):
     lib.orda_debug_gemm.argtypes = [_i32, _i32, _i32, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _vp, _vp]
     lib.orda_debug_gemm_pair.restype = _i32
     lib.orda_debug_gemm_pair.argtypes = lib.orda_debug_gemm.argtypes
+    lib.orda_debug_gemm_wide.restype = _i32
+    lib.orda_debug_gemm_wide.argtypes = lib.orda_debug_gemm.argtypes
+    lib.orda_debug_gemm_profile.restype = _i32
+    lib.orda_debug_gemm_profile.argtypes = [ctypes.c_void_p, _i32]
 
 
 def load(path: str | None = None):

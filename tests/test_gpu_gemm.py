@@ -7,7 +7,7 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def _run(dtype, a_mn, b_mn, M, N, K, seed=0, pair=False):
+def _run(dtype, a_mn, b_mn, M, N, K, seed=0, pair=False, wide=False):
     from orda_ce_kernel import _native
 
     lib = _native.load()
@@ -20,7 +20,7 @@ def _run(dtype, a_mn, b_mn, M, N, K, seed=0, pair=False):
     out = torch.full((M, N), float("nan"), device="cuda", dtype=torch.float32)
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     code = {torch.bfloat16: _native.BF16, torch.float16: _native.F16}[dtype]
-    fn = lib.orda_debug_gemm_pair if pair else lib.orda_debug_gemm
+    fn = lib.orda_debug_gemm_wide if wide else (lib.orda_debug_gemm_pair if pair else lib.orda_debug_gemm)
     rc = fn(code, int(a_mn), int(b_mn), a_store.data_ptr(), a_store.stride(0),
                              b_store.data_ptr(), b_store.stride(0), M, N, K, out.data_ptr(), out.stride(0),
                              status.data_ptr(), torch.cuda.current_stream().cuda_stream)
@@ -70,4 +70,21 @@ def test_pair_gemm_layouts(dtype, a_mn, b_mn, shape):
     if not a_mn and K % 8:
         K += 8 - K % 8
     out, ref = _run(dtype, a_mn, b_mn, M, N, K, seed=5, pair=True)
+    torch.testing.assert_close(out, ref, rtol=2e-3, atol=2e-3)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
+@pytest.mark.parametrize("shape", [(512, 512, 256), (520, 264, 1000), (1, 40, 8), (2048, 4096, 512), (1536, 768, 64)])
+def test_wide_gemm_layouts(dtype, a_mn, b_mn, shape):
+    """Wide CTA-pair kernel (512 x 256 tiles, two accumulators, split accumulator release): every
+    operand layout; ragged shapes; K shorter than the pipeline (a single k block)."""
+    M, N, K = shape
+    if a_mn and M % 8:
+        M += 8 - M % 8
+    if b_mn and N % 8:
+        N += 8 - N % 8
+    if not a_mn and K % 8:
+        K += 8 - K % 8
+    out, ref = _run(dtype, a_mn, b_mn, M, N, K, seed=7, wide=True)
     torch.testing.assert_close(out, ref, rtol=2e-3, atol=2e-3)
