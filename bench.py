@@ -36,6 +36,7 @@ REF_DIR = os.path.join(ROOT, "baseline", "_ref")
 METRIC = "fused CE+KL fwd+bwd tokens/sec at Llama-3-8B shape; % bf16 tensor peak; 1/2/4/8 GPU"
 N_TOK, HID, VOCAB = 8192, 4096, 128256
 CPU_ROWS = 256
+DEFAULT_RESERVE_SMS = 16  # SMs left to NCCL while the dHidden GEMM overlaps the dW all-reduce
 
 
 def _args():
@@ -48,6 +49,8 @@ def _args():
     p.add_argument("--rows", type=int, default=N_TOK, help="tokens per GPU")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--reserve-sms", type=int, default=-1,
+                   help="SMs the dHidden GEMM leaves to the overlapped dW all-reduce (N>1; -1: default)")
     return p.parse_args()
 
 
@@ -284,10 +287,13 @@ def run_ours(args):
 
     done = primed(torch.cuda.Event()) if pg is not None else None
 
+    reserve = (args.reserve_sms if args.reserve_sms >= 0 else DEFAULT_RESERVE_SMS) if pg is not None else 0
+
     def step(h, t, lab, events=None):
         h.grad = None
         w.grad = None
-        with _fused.instrument(phase_events=events, dweight_done_event=done, dweight_first=pg is not None):
+        with _fused.instrument(phase_events=events, dweight_done_event=done, dweight_first=pg is not None,
+                               reserve_sms=reserve):
             out = ok.distillation_loss(h, w, lab, ok.TiedTeacher(t), **kw)
             out.loss.backward()
         if pg is not None:
@@ -399,6 +405,7 @@ def run_ours(args):
                             "V=128256, forward KL (T=1, weight 1), teacher CE 1.0, dHidden + dW",
                 "tokens_per_gpu": rows, "hidden": HID, "vocab": VOCAB, "divergence": args.divergence,
                 "parallelism": f"token-sharded dp{world}" if world > 1 else "single GPU",
+                "overlap_reserve_sms": reserve,
                 "l2": "inputs larger than L2 (lm_head 1.05 GB, logits workspace 4.2 GB)",
             },
             "tflops_per_gpu": step_tf,

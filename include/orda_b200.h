@@ -134,6 +134,9 @@ typedef struct orda_distill_args {
   int32_t dweight_first;        /* run the dW GEMMs before the dH GEMMs (overlap the dW all-reduce)  */
   int32_t grads_include_mean_scale; /* 1: gradients already include out_reduced[ORDA_OUT_MEAN_SCALE]
                                    (1/count for mean), so backward only multiplies by grad_output     */
+  int32_t overlap_reserve_sms;  /* with dweight_first: the dHidden GEMMs, which run while the caller's
+                                   dW all-reduce runs on another stream, leave this many SMs free for
+                                   the collective's kernels (0 = use every SM)                        */
 } orda_distill_args_t;
 
 /* phases bracketed by phase_events */

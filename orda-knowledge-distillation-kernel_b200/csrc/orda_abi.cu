@@ -215,7 +215,8 @@ bool gemm_profiling() {
 }
 
 template <bool A_MN, bool B_MN, int AMODE, bool TWO_SEG, int EPI, typename T16>
-int launch_tc2(TcGemmParams& prm, int64_t M_tiles, int64_t N, cudaStream_t stream, int group_m) {
+int launch_tc2(TcGemmParams& prm, int64_t M_tiles, int64_t N, cudaStream_t stream, int group_m,
+               int reserve_sms = 0) {
   using S = PairShape<AMODE>;
   prm.m_tiles = static_cast<int32_t>(M_tiles);
   prm.n_tiles = static_cast<int32_t>(cdiv(N, kPairBN));
@@ -226,7 +227,8 @@ int launch_tc2(TcGemmParams& prm, int64_t M_tiles, int64_t N, cudaStream_t strea
   auto k = tc2_gemm_kernel<A_MN, B_MN, AMODE, TWO_SEG, EPI, T16>;
   set_smem(k, S::kSmemBytes);
   prm.prof_slot = gemm_profiling() ? (EPI == EPI_FWD_STATS ? 0 : (A_MN ? 2 : 1)) : -1;
-  const int pairs = static_cast<int>(std::min<int64_t>(tiles, num_sms() / 2));
+  const int usable = std::max(2, num_sms() - std::max(0, reserve_sms));
+  const int pairs = static_cast<int>(std::min<int64_t>(tiles, usable / 2));
   count_launch();
   k<<<2 * pairs, kGemmThreads, S::kSmemBytes, stream>>>(prm);
   return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
@@ -345,6 +347,7 @@ int forward_tc(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const C
 template <typename T16>
 int dh_tc(const orda_distill_args_t* a, const Plan& P, const void* dz, const void* wmat, int64_t ldw, int64_t n,
           void* out, int64_t rows, int32_t* status, cudaStream_t s) {
+  const int reserve = a->dweight_first ? a->overlap_reserve_sms : 0;
   TcGemmParams prm{};
   prm.status = status;
   int rc;
@@ -352,7 +355,7 @@ int dh_tc(const orda_distill_args_t* a, const Plan& P, const void* dz, const voi
   if ((rc = make_operand_map(&prm.b0, a->compute_dtype, wmat, true, n, a->vocab, ldw, 128))) return rc;
   prm.kb0 = static_cast<int32_t>(cdiv(a->vocab, kBK));
   prm.st = StoreEpiParams{out, n, rows, n, 0, 0};
-  return launch_tc2<false, true, A_PLAIN, false, EPI_STORE, T16>(prm, cdiv(rows, 256), n, s, 8);
+  return launch_tc2<false, true, A_PLAIN, false, EPI_STORE, T16>(prm, cdiv(rows, 256), n, s, 8, reserve);
 }
 
 // dW[V, N] (+)= dZ0^T H0 (+ dZ1^T H1)

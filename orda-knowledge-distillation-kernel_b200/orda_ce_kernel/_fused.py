@@ -39,13 +39,14 @@ _HOOKS = threading.local()
 
 
 @contextlib.contextmanager
-def instrument(phase_events=None, dweight_done_event=None, dweight_first=False):
+def instrument(phase_events=None, dweight_done_event=None, dweight_first=False, reserve_sms=0):
     """Attach CUDA events to the fused calls made inside the block (benchmarks / overlap):
     ``phase_events`` - 2*PHASES ``torch.cuda.Event(enable_timing=True)`` recorded around each phase;
     ``dweight_done_event`` - recorded when the weight gradients are complete;
-    ``dweight_first`` - run the dW GEMMs before the dH GEMMs."""
+    ``dweight_first`` - run the dW GEMMs before the dH GEMMs;
+    ``reserve_sms`` - with ``dweight_first``, SMs the dH GEMMs leave free for a concurrent all-reduce."""
     prev = getattr(_HOOKS, "value", None)
-    _HOOKS.value = (phase_events, dweight_done_event, dweight_first)
+    _HOOKS.value = (phase_events, dweight_done_event, dweight_first, reserve_sms)
     try:
         yield
     finally:
@@ -261,7 +262,7 @@ def launch_prepared(pr: Prepared, spec: FusedSpec, keep_alive=None) -> None:
     a, dev, status = pr.args, pr.dev, pr.status
     hooks = getattr(_HOOKS, "value", None)
     if hooks is not None:
-        ev, done, first = hooks
+        ev, done, first, reserve = hooks
         if ev is not None:
             handles = (ctypes.c_void_p * (2 * _native.PHASES))(*[e.cuda_event for e in ev])
             if keep_alive is not None:
@@ -270,6 +271,7 @@ def launch_prepared(pr: Prepared, spec: FusedSpec, keep_alive=None) -> None:
         if done is not None:
             a.dweight_done_event = done.cuda_event
         a.dweight_first = int(bool(first))
+        a.overlap_reserve_sms = int(reserve)
 
     ws_bytes = int(lib.orda_distill_workspace_bytes(a))
     ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)

@@ -74,6 +74,7 @@ class DistillArgs(ctypes.Structure):
         ("dweight_done_event", _vp),
         ("dweight_first", _i32),
         ("grads_include_mean_scale", _i32),
+        ("overlap_reserve_sms", _i32),
     ]
 
 
