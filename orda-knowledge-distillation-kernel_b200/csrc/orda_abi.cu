@@ -100,6 +100,9 @@ struct Plan {
   // layout
   int64_t C, n_vtiles, vpad;
   size_t off_row_losses, off_tile_stats, off_label, off_row_stats, off_row_sums, off_ws_s, off_ws_t, total;
+  int32_t parts;       // column parts of the row sweeps
+  int64_t part_cols;
+  size_t off_part_records;
 };
 
 int check_args(const orda_distill_args_t* a) {
@@ -173,6 +176,12 @@ Plan make_plan(const orda_distill_args_t* a, int64_t chunk_override) {
   p.off_label = off; off = align256(off + sizeof(float) * 2 * p.C);
   p.off_row_stats = off; off = align256(off + sizeof(float) * kRowStats * p.C);
   p.off_row_sums = off; off = align256(off + sizeof(float) * 2 * p.C);
+  // Row sweeps split long rows into up to 4 column parts (>= 16384 columns each) so that the warp
+  // tasks spread evenly over the SMs; the parts' records are merged like vocab shards.
+  p.parts = static_cast<int32_t>(std::max<int64_t>(1, std::min<int64_t>(4, a->vocab / 16384)));
+  p.part_cols = cdiv(cdiv(a->vocab, p.parts), 256) * 256;
+  p.off_part_records = off;
+  if (p.parts > 1) off = align256(off + sizeof(float) * kRowStats * p.parts * p.C);
   // the fp32 path materialises raw logits, so it always needs the student (and teacher) buffer
   const bool need_s = p.write_ws_s || a->compute_dtype == ORDA_F32;
   const bool need_t = p.teacher_acc && (p.write_ws_t || a->compute_dtype == ORDA_F32);
@@ -284,6 +293,9 @@ RowParams row_params(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, c
   r.t_gmem = c.tg; r.ld_tg = a->ld_teacher_logits; r.tg_dtype = a->teacher_logits_dtype;
   r.status = a->device_status;
   r.grad_scale = a->grads_include_mean_scale ? a->out_reduced + ORDA_OUT_MEAN_SCALE : nullptr;
+  r.parts = P.parts;
+  r.part_cols = P.part_cols;
+  r.part_records = reinterpret_cast<float*>(ws + P.off_part_records);
   return r;
 }
 
@@ -416,18 +428,24 @@ template <typename WsT>
 int row_phases(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const ChunkPtrs& c, cudaStream_t s,
                bool do_merge, bool do_loss_and_sweeps, const float* row_stats_ext, const float* row_sums_ext) {
   RowParams r = row_params(a, P, ws, c);
-  // one warp per row, 8 rows per block
-  const int sweep_grid = static_cast<int>(std::min<int64_t>(cdiv(c.rows, 8), 16 * num_sms()));
+  // one warp per (row, column part), 8 per block; the JSD sweep runs one warp per row
+  const int sweep_grid = static_cast<int>(std::min<int64_t>(cdiv(c.rows * P.parts, 8), 16 * num_sms()));
+  const int row_grid = static_cast<int>(std::min<int64_t>(cdiv(c.rows, 8), 16 * num_sms()));
   if (do_merge) {
     count_launch();
     launch_row_stats<WsT>(r, sweep_grid, s);
+    if (P.parts > 1) {
+      count_launch();
+      merge_records_kernel<<<static_cast<int>(cdiv(c.rows, 256)), 256, 0, s>>>(r.part_records, P.parts, c.rows,
+                                                                              r.row_stats);
+    }
   }
   if (!do_loss_and_sweeps) return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
   if (row_stats_ext) r.row_stats = const_cast<float*>(row_stats_ext);
   if (P.jsd && !row_sums_ext) {
     float* sums = reinterpret_cast<float*>(ws + P.off_row_sums);
     count_launch();
-    jsd_sweep_kernel<WsT><<<sweep_grid, 256, 0, s>>>(r, sums);
+    jsd_sweep_kernel<WsT><<<row_grid, 256, 0, s>>>(r, sums);
   }
   if (row_sums_ext) r.row_sums = row_sums_ext;
   count_launch();

@@ -35,7 +35,20 @@ struct RowParams {
   const void* t_gmem; int64_t ld_tg; int32_t tg_dtype;
   int32_t* status;
   const float* grad_scale;  // optional device scalar multiplying the dlogits (1/count for mean)
+  // Column parts: each row is swept as `parts` column ranges of `part_cols` (a multiple of 256)
+  // handled by different warps, so that the number of warp tasks balances over the SMs. With
+  // parts > 1 row_stats writes one record per part into part_records[part][rows][kRowStats]; the
+  // records are merged like vocab shards.
+  int32_t parts;
+  int64_t part_cols;
+  float* part_records;
 };
+
+// Column range [c0, c1) of part `part` of a row.
+__device__ __forceinline__ void part_range(const RowParams& p, int part, int64_t& c0, int64_t& c1) {
+  c0 = static_cast<int64_t>(part) * p.part_cols;
+  c1 = c0 + p.part_cols < p.vocab ? c0 + p.part_cols : p.vocab;
+}
 
 __device__ __forceinline__ Partial warp_merge(Partial a, double inv_t, bool cross) {
 #pragma unroll
@@ -238,10 +251,16 @@ __global__ void __launch_bounds__(256) row_stats_kernel(RowParams p) {
   const float it = p.inv_t;
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
-  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; row < p.rows; row += warps) {
+  const int64_t tasks = p.rows * p.parts;
+  for (int64_t task = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; task < tasks; task += warps) {
+    const int64_t row = task / p.parts;
+    const int part = static_cast<int>(task - row * p.parts);
+    int64_t c0, c1;
+    part_range(p, part, c0, c1);
     const float2* tm = row_tile_maxima(p, row);
     float lms = -CUDART_INF_F, lmt = -CUDART_INF_F;
-    for (int i = lane; i < p.n_vtiles; i += 32) {
+    const int t1 = static_cast<int>((c1 + kVocabTile - 1) / kVocabTile);
+    for (int i = static_cast<int>(c0 / kVocabTile) + lane; i < t1; i += 32) {
       const float2 m = __ldg(tm + i);
       lms = fmaxf(lms, m.x);
       lmt = fmaxf(lmt, m.y);
@@ -251,11 +270,11 @@ __global__ void __launch_bounds__(256) row_stats_kernel(RowParams p) {
     float s1s[2] = {0.f, 0.f}, sts[2] = {0.f, 0.f}, s1t[2] = {0.f, 0.f}, stt[2] = {0.f, 0.f}, cross[2] = {0.f, 0.f};
     const WsT* rs = static_cast<const WsT*>(p.ws_s) + row * p.ld_ws;
     const WsT* rt = static_cast<const WsT*>(p.ws_t) + row * p.ld_ws;
-    for (int64_t j0 = (int64_t)lane * 8; j0 < p.vocab; j0 += 256) {
+    for (int64_t j0 = c0 + (int64_t)lane * 8; j0 < c1; j0 += 256) {
       const float2 m = __ldg(tm + j0 / kVocabTile);
       float ds[8], u[8];
       load8<WsT>(rs + j0, ds);
-      const int cnt = p.vocab - j0 < 8 ? static_cast<int>(p.vocab - j0) : 8;
+      const int cnt = c1 - j0 < 8 ? static_cast<int>(c1 - j0) : 8;
       if constexpr (TSRC == TS_GMEM) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) u[j] = j < cnt ? load_tg(p, row, j0 + j) : -CUDART_INF_F;
@@ -320,11 +339,12 @@ __global__ void __launch_bounds__(256) row_stats_kernel(RowParams p) {
       T = Partial{mt, warp_sum(s1t[0] + s1t[1]), warp_sum(stt[0] + stt[1]), rev ? 0.0 : (double)warp_sum(cr)};
     }
     if (lane == 0) {
-      float* out = p.row_stats + row * kRowStats;
+      float* out = p.parts == 1 ? p.row_stats + row * kRowStats
+                                : p.part_records + (static_cast<int64_t>(part) * p.rows + row) * kRowStats;
       bool ignored;
       const int64_t ys = safe_label(p.labels[row], p.ignore_index, p.vocab_total, &ignored);
-      const bool has = !ignored && ys >= p.vocab_offset && ys < p.vocab_offset + p.vocab;
-      if (f & F_VALIDATE) {  // validate labels (debug profile): flag, never trap
+      const bool has = !ignored && ys >= p.vocab_offset + c0 && ys < p.vocab_offset + c1;
+      if ((f & F_VALIDATE) && part == 0) {  // validate labels (debug profile): flag, never trap
         const int64_t y = p.labels[row];
         if (y != p.ignore_index && (y < 0 || y >= p.vocab_total)) atomicCAS(p.status, 0, ORDA_ERR_LABEL_RANGE);
       }
@@ -359,7 +379,11 @@ __global__ void __launch_bounds__(256) jsd_sweep_kernel(RowParams p, float* row_
   const float beta = p.jsd_beta, lb = logf(beta), l1b = log1pf(-beta), it = p.inv_t;
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
-  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; row < p.rows; row += warps) {
+  const int64_t tasks = p.rows * p.parts;
+  for (int64_t task = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; task < tasks; task += warps) {
+    const int64_t row = task / p.parts;
+    int64_t c0, c1;
+    part_range(p, static_cast<int>(task - row * p.parts), c0, c1);
     const float2* tm = row_tile_maxima(p, row);
     const RowConsts c = row_consts(p, row);
     float acc_j = 0.f, acc_g = 0.f;
@@ -403,7 +427,11 @@ __global__ void __launch_bounds__(256) grad_sweep_kernel(RowParams p) {
   const bool need_t = TSRC != TS_NONE && (kl || grad_t);
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
-  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; row < p.rows; row += warps) {
+  const int64_t tasks = p.rows * p.parts;
+  for (int64_t task = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; task < tasks; task += warps) {
+    const int64_t row = task / p.parts;
+    int64_t c0, c1;
+    part_range(p, static_cast<int>(task - row * p.parts), c0, c1);
     const float2* tm = row_tile_maxima(p, row);
     const RowConsts c = row_consts(p, row);
     float rrev = 0.f, gsum = 0.f;
@@ -415,7 +443,7 @@ __global__ void __launch_bounds__(256) grad_sweep_kernel(RowParams p) {
     const float gscale = p.grad_scale ? *p.grad_scale : 1.f;
     WsT* rs = static_cast<WsT*>(p.ws_s) + row * p.ld_ws;
     WsT* rt = static_cast<WsT*>(p.ws_t) + row * p.ld_ws;
-    for (int64_t j0 = (int64_t)lane * 8; j0 < p.vocab; j0 += 256) {
+    for (int64_t j0 = c0 + (int64_t)lane * 8; j0 < c1; j0 += 256) {
       float gs[8], gt[8];
       if (c.ignored) {
 #pragma unroll

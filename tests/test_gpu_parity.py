@@ -426,3 +426,29 @@ def test_backward_scales_by_grad_output_and_supports_retain_graph():
     assert _rel_err(hs.grad, ref.d_student_hidden) < 2e-2
     torch.testing.assert_close(hs.grad.float() * 3.0, g_hs.float(), rtol=2e-2, atol=1e-6)
     torch.testing.assert_close(weight.grad.float() * 3.0, g_w.float(), rtol=2e-2, atol=1e-6)
+
+
+# ----------------------------------------------------------------- row sweeps split into column parts
+@pytest.mark.parametrize("mode", ["tied", "separate-full", "precomputed-logits"])
+@pytest.mark.parametrize("div", ["forward", "reverse", "jsd"])
+def test_row_sweeps_in_column_parts(mode, div):
+    """V >= 32768 splits each row's sweeps into column parts whose records are merged like vocab
+    shards; V = 50000 gives 3 parts with a ragged last part and labels in every part."""
+    hs, weight, labels, teacher, tce, kw = _llm_inputs(mode, seed=71, BT=96, H=128, Ht=192, V=50000)
+    labels[1::3] = torch.arange(labels[1::3].numel(), device=labels.device) * 997 % 50000
+    if mode == "precomputed-logits":
+        g = torch.Generator().manual_seed(72)
+        tl = torch.log_softmax(torch.randn(*labels.shape, weight.shape[0], generator=g) * 2.0, -1).cuda()
+        teacher = PrecomputedTeacher(logits=tl)
+        kw = dict(mode="precomputed", teacher_logits=tl)
+    loss_kw = dict(teacher_ce_weight=tce, student_ce_weight=0.5, kl_weight=0.5, kl_temperature=1.5,
+                   kl_divergence=div)
+    out = distillation_loss(hs, weight, labels, teacher, **loss_kw)
+    out.loss.backward()
+    ref = _oracle(hs, weight, labels, kw, **loss_kw)
+    _close(out.loss, ref.loss, atol=0.0, rtol=1e-3, name="loss")
+    _close(out.kl, ref.kl, atol=1e-5, rtol=1e-3, name="kl")
+    assert _rel_err(hs.grad, ref.d_student_hidden) < 2e-2
+    assert _rel_err(weight.grad, ref.d_weight) < 2e-2
+    if mode == "separate-full":
+        assert _rel_err(teacher.hidden.grad, ref.d_teacher_hidden) < 2e-2
