@@ -44,6 +44,15 @@ struct RowParams {
   float* part_records;
 };
 
+constexpr float kLog2e = 1.4426950408889634f;
+
+// 2^x with the hardware approximation (the same instruction __expf uses after scaling by log2 e).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Column range [c0, c1) of part `part` of a row.
 __device__ __forceinline__ void part_range(const RowParams& p, int part, int64_t& c0, int64_t& c1) {
   c0 = static_cast<int64_t>(part) * p.part_cols;
@@ -270,6 +279,42 @@ __global__ void __launch_bounds__(256) row_stats_kernel(RowParams p) {
     float s1s[2] = {0.f, 0.f}, sts[2] = {0.f, 0.f}, s1t[2] = {0.f, 0.f}, stt[2] = {0.f, 0.f}, cross[2] = {0.f, 0.f};
     const WsT* rs = static_cast<const WsT*>(p.ws_s) + row * p.ld_ws;
     const WsT* rt = static_cast<const WsT*>(p.ws_t) + row * p.ld_ws;
+    if constexpr (!TNO && TSRC != TS_GMEM) {
+      // T = 1: the tempered sums equal the plain ones. Exponents are formed in base 2 with one FMA
+      // from the stored shifted logits; the cross term is accumulated as w * (log2 difference) and
+      // converted once per lane: u - z = (tL - dL) / log2 e + (mt - Ms).
+      const bool want_t = teacher && (need_t1 || kl);
+      float es[2] = {0.f, 0.f}, et[2] = {0.f, 0.f}, cr[2] = {0.f, 0.f};
+      for (int64_t j0 = c0 + (int64_t)lane * 8; j0 < c1; j0 += 256) {
+        const float2 m = __ldg(tm + j0 / kVocabTile);
+        float ds[8], dt[8];
+        load8<WsT>(rs + j0, ds);
+        if (want_t) load8<WsT>(rt + j0, dt);
+        const int cnt = c1 - j0 < 8 ? static_cast<int>(c1 - j0) : 8;
+        const float offs = (m.x - Ms) * kLog2e, offt = (m.y - mt) * kLog2e;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int q = j & 1;
+          const bool valid = j < cnt;
+          const float dL = fmaf(ds[j], kLog2e, offs);
+          const float e = valid ? ex2_approx(dL) : 0.f;
+          es[q] += e;
+          if (want_t) {
+            const float tL = fmaf(dt[j], kLog2e, offt);
+            const float t = valid ? ex2_approx(tL) : 0.f;
+            et[q] += t;
+            if (kl) cr[q] += rev ? e * (dL - tL) : t * (tL - dL);
+          }
+        }
+      }
+      constexpr float kLn2 = 0.6931471805599453f;
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        s1s[q] = sts[q] = es[q];
+        s1t[q] = stt[q] = et[q];
+        cross[q] = !(want_t && kl) ? 0.f : rev ? cr[q] * kLn2 + (Ms - mt) * es[q] : cr[q] * kLn2 + (mt - Ms) * et[q];
+      }
+    } else
     for (int64_t j0 = c0 + (int64_t)lane * 8; j0 < c1; j0 += 256) {
       const float2 m = __ldg(tm + j0 / kVocabTile);
       float ds[8], u[8];
@@ -443,6 +488,59 @@ __global__ void __launch_bounds__(256) grad_sweep_kernel(RowParams p) {
     const float gscale = p.grad_scale ? *p.grad_scale : 1.f;
     WsT* rs = static_cast<WsT*>(p.ws_s) + row * p.ld_ws;
     WsT* rt = static_cast<WsT*>(p.ws_t) + row * p.ld_ws;
+    if constexpr (sizeof(WsT) == 2 && !TNO && (DK == DK_FWD || DK == DK_NONE) && TSRC != TS_GMEM) {
+      if (c.ignored) {
+        const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+        for (int64_t j0 = c0 + (int64_t)lane * 8; j0 < c1; j0 += 256) {
+          if (grad_s) *reinterpret_cast<uint4*>(rs + j0) = z;
+          if (grad_t) *reinterpret_cast<uint4*>(rt + j0) = z;
+        }
+        continue;  // next task
+      }
+      // T = 1, forward KL or none: p = 2^(stored * log2 e + per-tile constant), one FMA + one ex2 per
+      // distribution; dZ_s = (w_s + w_kl) p_s - w_kl p_t - w_s [label], dZ_t = w_t (p_t - [label]),
+      // all scaled by gscale.
+      const float kl_w = kl ? kls : 0.f;
+      const float as = gscale * (p.w_s + kl_w), bs = gscale * kl_w, at = gscale * p.w_t;
+      const float ys = gscale * p.w_s;
+      const float base_s = -(c.ms + c.log_s1) * kLog2e, base_t = -(c.mt + c.log_t1) * kLog2e;
+      for (int64_t j0 = c0 + (int64_t)lane * 8; j0 < c1; j0 += 256) {
+        const float2 m = __ldg(tm + j0 / kVocabTile);
+        float ds[8], dt[8];
+        load8<WsT>(rs + j0, ds);
+        if (need_t) load8<WsT>(rt + j0, dt);
+        const float cs = fmaf(m.x, kLog2e, base_s), ct = fmaf(m.y, kLog2e, base_t);
+        float gs[8], gt[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float ps = ex2_approx(fmaf(ds[j], kLog2e, cs));
+          const float pt = need_t ? ex2_approx(fmaf(dt[j], kLog2e, ct)) : 0.f;
+          gs[j] = fmaf(as, ps, -bs * pt);
+          gt[j] = at * pt;
+        }
+        const int64_t lc = c.label_local - j0;  // label column inside this vector of 8
+        if (lc >= 0 && lc < 8) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            if (j == lc) {
+              gs[j] -= ys;
+              gt[j] -= at;
+            }
+        }
+        if (grad_s) {
+          uint4 u;
+          u.x = pack2<WsT>(gs[0], gs[1]); u.y = pack2<WsT>(gs[2], gs[3]);
+          u.z = pack2<WsT>(gs[4], gs[5]); u.w = pack2<WsT>(gs[6], gs[7]);
+          *reinterpret_cast<uint4*>(rs + j0) = u;
+        }
+        if (grad_t) {
+          uint4 u;
+          u.x = pack2<WsT>(gt[0], gt[1]); u.y = pack2<WsT>(gt[2], gt[3]);
+          u.z = pack2<WsT>(gt[4], gt[5]); u.w = pack2<WsT>(gt[6], gt[7]);
+          *reinterpret_cast<uint4*>(rt + j0) = u;
+        }
+      }
+    } else {
     for (int64_t j0 = c0 + (int64_t)lane * 8; j0 < c1; j0 += 256) {
       float gs[8], gt[8];
       if (c.ignored) {
@@ -490,6 +588,7 @@ __global__ void __launch_bounds__(256) grad_sweep_kernel(RowParams p) {
       }
       if (grad_s) store8<WsT>(rs + j0, gs);
       if (grad_t) store8<WsT>(rt + j0, gt);
+    }
     }
   }
 }
