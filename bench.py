@@ -359,24 +359,42 @@ def run_ours(args):
     if not args.no_e2e:
         hs_p, ht_p, lab_p = hs_h.pin_memory(), ht_h.pin_memory(), lab_h.pin_memory()
         loss_host = torch.empty((), dtype=torch.float32).pin_memory()
-        hs_d = torch.empty_like(hs_h, device=dev)
-        ht_d = torch.empty_like(ht_h, device=dev)
-        lab_d = torch.empty_like(lab_h, device=dev)
+        # two device buffer sets: the host->device copy of step i+1 runs on a copy stream while step i
+        # computes (the usual input prefetch of a training loop); every step's copy is in the timed region
+        bufs = [(torch.empty_like(hs_h, device=dev), torch.empty_like(ht_h, device=dev),
+                 torch.empty_like(lab_h, device=dev)) for _ in range(2)]
+        copy_stream = torch.cuda.Stream(device=dev)
+        copied = [torch.cuda.Event() for _ in range(2)]
+        consumed = [primed(torch.cuda.Event()) for _ in range(2)]
 
-        def e2e_step():
-            hs_d.copy_(hs_p, non_blocking=True)
-            ht_d.copy_(ht_p, non_blocking=True)
-            lab_d.copy_(lab_p, non_blocking=True)
-            o = step(hs_d.detach().requires_grad_(True), ht_d, lab_d)
-            loss_host.copy_(o.loss.detach(), non_blocking=True)
+        def issue_copy(i):
+            b = bufs[i % 2]
+            copy_stream.wait_event(consumed[i % 2])  # step i-2 has finished reading this buffer set
+            with torch.cuda.stream(copy_stream):
+                b[0].copy_(hs_p, non_blocking=True)
+                b[1].copy_(ht_p, non_blocking=True)
+                b[2].copy_(lab_p, non_blocking=True)
+                copied[i % 2].record()
 
-        for _ in range(2):
-            e2e_step()
+        def e2e_run(n):
+            issue_copy(0)
+            for i in range(n):
+                if i + 1 < n:
+                    issue_copy(i + 1)
+                cur = torch.cuda.current_stream()
+                cur.wait_event(copied[i % 2])
+                b = bufs[i % 2]
+                o = step(b[0].detach().requires_grad_(True), b[1], b[2])
+                consumed[i % 2].record(cur)
+                loss_host.copy_(o.loss.detach(), non_blocking=True)
+
+        e2e_run(2)
         sync_all()
         s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s2.record()
-        for _ in range(K):
-            e2e_step()
+        copy_stream.wait_event(s2)  # no copy of the timed steps starts before the timed region
+        e2e_run(K)
+        torch.cuda.current_stream().wait_stream(copy_stream)
         e2.record()
         sync_all()
         ms_e2e = s2.elapsed_time(e2) / K
@@ -388,7 +406,7 @@ def run_ours(args):
             ms_e2e = float(t.item())
         e2e = {"value": world * rows / (ms_e2e / 1e3), "unit": "tokens/s",
                "h2d_bytes_per_step": hs_h.numel() * 2 + ht_h.numel() * 2 + lab_h.numel() * 8,
-               "d2h_bytes_per_step": 4}
+               "d2h_bytes_per_step": 4, "input_prefetch": "next step's H2D copy on a copy stream"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
