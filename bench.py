@@ -441,7 +441,7 @@ def run_ours(args):
             "clocks": clk.summary(),
             "e2e": e2e,
             "cpu_baseline": cpu,
-            "loss": float(out.loss),
+            "loss": float(out.loss.detach()),
         }
         print(json.dumps(line))
     if pg is not None:
