@@ -35,6 +35,7 @@ struct FwdEpiParams {
   int32_t tg_dtype;
   float* tile_stats;              // [rows][n_vtiles][kTileStats]
   float* label_logits;            // [rows][2]
+  int32_t plain_teacher;          // wide kernel, A_PLAIN: the accumulators hold teacher logits
 };
 
 template <typename WsT>

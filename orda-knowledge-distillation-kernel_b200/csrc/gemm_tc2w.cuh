@@ -361,8 +361,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
                               student, lane, j ? lab[1] : lab[0]);
           } else {
             const int64_t y0 = static_cast<int64_t>(mt) * 512 + j * 256 + rank * 128 + quarter * 32;
-            wide_fwd_acc<T16>(p.fwd, &p.ws_s_map, (p.fwd.flags & F_WRITE_WS_S) != 0, tbase, staging, y0 + lane, y0,
-                              n0, true, lane, j ? lab[1] : lab[0]);
+            const bool tdist = p.fwd.plain_teacher != 0;  // separate teacher: a second launch over (ht, Wt)
+            wide_fwd_acc<T16>(p.fwd, tdist ? &p.ws_t_map : &p.ws_s_map,
+                              (p.fwd.flags & (tdist ? F_WRITE_WS_T : F_WRITE_WS_S)) != 0, tbase, staging, y0 + lane,
+                              y0, n0, !tdist, lane, j ? lab[1] : lab[0]);
           }
         } else {
           const int64_t row = static_cast<int64_t>(mt) * 512 + j * 256 + rank * 128 + quarter * 32 + lane;

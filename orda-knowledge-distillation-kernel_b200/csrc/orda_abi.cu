@@ -345,14 +345,20 @@ int forward_tc(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const C
     if ((rc = ws_store_maps(a, P, ws, c, prm))) return rc;
     return launch_tc2w<false, false, A_INTERLEAVE, false, EPI_FWD_STATS, T16>(prm, cdiv(c.rows, 256), a->vocab, s, 8);
   }
-  if (P.teacher_acc) {
-    if ((rc = make_operand_map(&prm.a1, dt, c.ht, false, c.rows, a->teacher_hidden, a->ld_teacher_hidden, kTileRows))) return rc;
-    if ((rc = make_operand_map(&prm.b1, dt, a->teacher_weight, false, a->vocab, a->teacher_hidden, a->ld_teacher_weight, kVocabTile))) return rc;
-    prm.kb1 = static_cast<int32_t>(cdiv(a->teacher_hidden, kBK));
-    return launch_tc<kVocabTile, false, false, GM_TWO_ACC, EPI_FWD_STATS, T16>(prm, c.rows, a->vocab, s, 16);
-  }
   if ((rc = ws_store_maps(a, P, ws, c, prm))) return rc;
-  return launch_tc2w<false, false, A_PLAIN, false, EPI_FWD_STATS, T16>(prm, cdiv(c.rows, 512), a->vocab, s, 4);
+  if ((rc = launch_tc2w<false, false, A_PLAIN, false, EPI_FWD_STATS, T16>(prm, cdiv(c.rows, 512), a->vocab, s, 4)))
+    return rc;
+  if (P.teacher_acc) {
+    // separate teacher (or precomputed teacher hidden + weight): a second wide launch over (ht, Wt)
+    // writes the teacher's tile maxima, shifted logits and label logits
+    TcGemmParams pt = prm;
+    if ((rc = make_operand_map(&pt.a0, dt, c.ht, false, c.rows, a->teacher_hidden, a->ld_teacher_hidden, kTileRows))) return rc;
+    if ((rc = make_operand_map(&pt.b0, dt, a->teacher_weight, false, a->vocab, a->teacher_hidden, a->ld_teacher_weight, kVocabTile))) return rc;
+    pt.kb0 = static_cast<int32_t>(cdiv(a->teacher_hidden, kBK));
+    pt.fwd.plain_teacher = 1;
+    return launch_tc2w<false, false, A_PLAIN, false, EPI_FWD_STATS, T16>(pt, cdiv(c.rows, 512), a->vocab, s, 4);
+  }
+  return ORDA_OK;
 }
 
 // dH[rows, N] = dZ[rows, V] * Wm[V, N]
