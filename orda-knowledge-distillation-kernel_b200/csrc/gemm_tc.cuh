@@ -7,15 +7,10 @@
 // Two TMEM accumulator buffers let the epilogue of tile i overlap the mainloop of tile i+1.
 // Operands are bf16 or fp16; each may be K-major (k contiguous) or MN-major (m / n contiguous),
 // which covers the three GEMMs of the loss: logits = H W^T (K/K), dH = dZ W (K/MN),
-// dW = dZ^T H (MN/MN).
-//
-// Modes:
-//   GM_SINGLE        one operand pair, one accumulator
-//   GM_SHARED_B      tied teacher: A0 (student rows) and A1 (teacher rows) share each B (lm_head)
-//                    tile; two accumulators (student, teacher) - the lm_head is streamed once
-//   GM_TWO_ACC       separate teacher: (A0, B0) over K0 then (A1, B1) over K1, two accumulators
-//   GM_TWO_SEG       (A0, B0) over K0 then (A1, B1) over K1 into ONE accumulator
-//                    (dW of the tied teacher: dZ_s^T H_s + dZ_t^T H_t)
+// dW = dZ^T H (MN/MN). The loss itself runs on the CTA-pair kernels (gemm_tc2.cuh, gemm_tc2w.cuh);
+// this single-CTA kernel is the reference GEMM of the layout tests (orda_debug_gemm). This header
+// also holds the parameter block, the operand descriptors, the tile rasterisation and the store
+// epilogue that the pair kernels share.
 // No cluster launch and no multicast: every CTA loads its own tiles.
 #pragma once
 
@@ -25,7 +20,6 @@
 
 namespace orda {
 
-enum GemmMode { GM_SINGLE = 0, GM_SHARED_B = 1, GM_TWO_ACC = 2, GM_TWO_SEG = 3 };
 enum EpiKind { EPI_FWD_STATS = 0, EPI_STORE = 1 };
 
 constexpr int kBK = 64;                       // k elements per stage (128 B of 16-bit data)
@@ -53,14 +47,12 @@ struct TcGemmParams {
   StoreEpiParams st;
 };
 
-template <int BN, int MODE>
+template <int BN>
 struct GemmShape {
-  static constexpr int kNumA = (MODE == GM_SHARED_B) ? 2 : 1;
-  static constexpr int kNumAcc = (MODE == GM_SHARED_B || MODE == GM_TWO_ACC) ? 2 : 1;
   static constexpr uint32_t kBBytes = BN * kBK * 2;
-  static constexpr uint32_t kStageBytes = kNumA * kATileBytes + kBBytes;
+  static constexpr uint32_t kStageBytes = kATileBytes + kBBytes;
   static constexpr int kStages = (kSmemBudget / kStageBytes) > 8 ? 8 : (kSmemBudget / kStageBytes);
-  static constexpr uint32_t kAccCols = kNumAcc * BN;  // one accumulator buffer
+  static constexpr uint32_t kAccCols = BN;  // one accumulator buffer
   static constexpr uint32_t kTmemCols = 2 * kAccCols;
   static constexpr uint32_t kBarBytes = (2 * kStages + 4) * 8 + 16;
   static constexpr uint32_t kSmemBytes = kStages * kStageBytes + kBarBytes + 1024;
@@ -110,15 +102,6 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t base, int kk) {
   if constexpr (MN) return smem_desc_sw128(base + kk * 2048u, 8192u, 1024u);
   else return smem_desc_sw128(base + kk * 32u, 16u, 1024u);
 }
-
-// TMEM-backed source of accumulator chunks for the statistics epilogue.
-template <int BN>
-struct TmemSrc {
-  uint32_t base;  // lane offset + accumulator buffer column
-  __device__ __forceinline__ void load(int acc, int chunk, float (&v)[32]) const {
-    tmem_ld32(base + acc * BN + chunk * 32, v);
-  }
-};
 
 template <typename T16>
 __device__ __forceinline__ void store_epilogue(const StoreEpiParams& st, uint32_t tbase, int64_t row, int64_t n0,
@@ -172,9 +155,9 @@ __device__ __forceinline__ void store_epilogue(const StoreEpiParams& st, uint32_
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, int MODE, int EPI, typename T16>
+template <int BN, bool A_MN, bool B_MN, typename T16>
 __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
-  using S = GemmShape<BN, MODE>;
+  using S = GemmShape<BN>;
   constexpr uint32_t kIdesc =
       make_idesc_f16(sizeof(T16) == 2 && std::is_same<T16, __nv_bfloat16>::value ? 1u : 0u, kTileRows, BN,
                      A_MN ? 1u : 0u, B_MN ? 1u : 0u);
@@ -193,7 +176,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const int32_t num_tiles = p.m_tiles * p.n_tiles;
-  const int32_t kb_total = (MODE == GM_TWO_ACC || MODE == GM_TWO_SEG) ? p.kb0 + p.kb1 : p.kb0;
+  const int32_t kb_total = p.kb0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S::kStages; ++s) {
@@ -209,10 +192,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&p.a0);
     tma_prefetch_desc(&p.b0);
-    if (MODE != GM_SINGLE) {
-      tma_prefetch_desc(&p.a1);
-      if (MODE != GM_SHARED_B) tma_prefetch_desc(&p.b1);
-    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, S::kTmemCols);
@@ -236,18 +215,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
         for (int32_t kb = 0; kb < kb_total; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.status)) { ok = false; break; }
           const uint32_t sa = tiles_addr + stage * S::kStageBytes;
-          const uint32_t sb = sa + S::kNumA * kATileBytes;
+          const uint32_t sb = sa + kATileBytes;
           mbar_arrive_expect_tx(full_bar(stage), S::kStageBytes);
-          if (MODE == GM_SHARED_B) {
-            load_operand<A_MN>(sa, &p.a0, full_bar(stage), m0, kb * kBK, kTileRows);
-            load_operand<A_MN>(sa + kATileBytes, &p.a1, full_bar(stage), m0, kb * kBK, kTileRows);
-            load_operand<B_MN>(sb, &p.b0, full_bar(stage), n0, kb * kBK, BN);
-          } else {
-            const bool seg1 = (MODE == GM_TWO_ACC || MODE == GM_TWO_SEG) && kb >= p.kb0;
-            const int32_t k0 = (seg1 ? kb - p.kb0 : kb) * kBK;
-            load_operand<A_MN>(sa, seg1 ? &p.a1 : &p.a0, full_bar(stage), m0, k0, kTileRows);
-            load_operand<B_MN>(sb, seg1 ? &p.b1 : &p.b0, full_bar(stage), n0, k0, BN);
-          }
+          load_operand<A_MN>(sa, &p.a0, full_bar(stage), m0, kb * kBK, kTileRows);
+          load_operand<B_MN>(sb, &p.b0, full_bar(stage), n0, kb * kBK, BN);
           if (++stage == S::kStages) { stage = 0; phase ^= 1u; }
         }
       }
@@ -269,17 +240,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
           if (!mbar_wait(full_bar(stage), phase, p.status)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = tiles_addr + stage * S::kStageBytes;
-          const uint32_t sb = sa + S::kNumA * kATileBytes;
-          const bool seg1 = (MODE == GM_TWO_ACC || MODE == GM_TWO_SEG) && kb >= p.kb0;
-          const int32_t kb_in_seg = seg1 ? kb - p.kb0 : kb;
-          const uint32_t d = (MODE == GM_TWO_ACC && seg1) ? acc0 + BN : acc0;
+          const uint32_t sb = sa + kATileBytes;
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint64_t bdesc = operand_desc<B_MN>(sb, kk);
-            const uint32_t accum = (MODE == GM_TWO_SEG) ? ((kb | kk) != 0) : ((kb_in_seg | kk) != 0);
-            tc_mma_f16(d, operand_desc<A_MN>(sa, kk), bdesc, kIdesc, accum);
-            if (MODE == GM_SHARED_B) tc_mma_f16(acc0 + BN, operand_desc<A_MN>(sa + kATileBytes, kk), bdesc, kIdesc, accum);
-          }
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            tc_mma_f16(acc0, operand_desc<A_MN>(sa, kk), operand_desc<B_MN>(sb, kk), kIdesc, (kb | kk) != 0);
           tc_commit(empty_bar(stage));
           if (++stage == S::kStages) { stage = 0; phase ^= 1u; }
         }
@@ -300,13 +264,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
       tile_coords(t, p.m_tiles, p.n_tiles, p.group_m, mt, nt);
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * S::kAccCols;
       const int64_t row = static_cast<int64_t>(mt) * kTileRows + r;
-      if constexpr (EPI == EPI_FWD_STATS) {
-        static_assert(BN == kVocabTile, "statistics epilogue expects 128-column vocab tiles");
-        TmemSrc<BN> src{tbase};
-        fwd_tile_stats<T16, S::kNumAcc == 2>(p.fwd, row, row < p.fwd.rows, static_cast<int64_t>(nt) * BN, nt, src);
-      } else {
-        store_epilogue<T16>(p.st, tbase, row, static_cast<int64_t>(nt) * BN, BN);
-      }
+      store_epilogue<T16>(p.st, tbase, row, static_cast<int64_t>(nt) * BN, BN);
       tc_fence_before();
       mbar_arrive(tempty_bar(buf));
     }

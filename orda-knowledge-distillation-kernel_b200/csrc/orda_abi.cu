@@ -196,16 +196,16 @@ void set_smem(Kernel k, uint32_t bytes) {
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
 }
 
-template <int BN, bool A_MN, bool B_MN, int MODE, int EPI, typename T16>
+template <int BN, bool A_MN, bool B_MN, typename T16>
 int launch_tc(TcGemmParams& prm, int64_t M, int64_t N, cudaStream_t stream, int group_m) {
-  using S = GemmShape<BN, MODE>;
+  using S = GemmShape<BN>;
   prm.m_tiles = static_cast<int32_t>(cdiv(M, kTileRows));
   prm.n_tiles = static_cast<int32_t>(cdiv(N, BN));
   prm.group_m = group_m;
   const int64_t tiles = (int64_t)prm.m_tiles * prm.n_tiles;
   if (tiles <= 0) return ORDA_OK;
   if (tiles > INT32_MAX) return ORDA_ERR_UNSUPPORTED;
-  auto k = tc_gemm_kernel<BN, A_MN, B_MN, MODE, EPI, T16>;
+  auto k = tc_gemm_kernel<BN, A_MN, B_MN, T16>;
   set_smem(k, S::kSmemBytes);
   const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms()));
   count_launch();
@@ -792,7 +792,7 @@ int32_t orda_debug_gemm(int32_t dtype, int32_t a_mn, int32_t b_mn, const void* A
   prm.kb0 = static_cast<int32_t>(cdiv(K, kBK));
   prm.st = StoreEpiParams{out, ldo, M, N, 1, 0};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-#define ORDA_DBG(T, AM, BM) return launch_tc<256, AM, BM, GM_SINGLE, EPI_STORE, T>(prm, M, N, s, 8)
+#define ORDA_DBG(T, AM, BM) return launch_tc<256, AM, BM, T>(prm, M, N, s, 8)
   if (dtype == ORDA_BF16) {
     if (a_mn && b_mn) ORDA_DBG(__nv_bfloat16, true, true);
     if (a_mn) ORDA_DBG(__nv_bfloat16, true, false);
