@@ -32,12 +32,16 @@ namespace orda {
 
 constexpr uint32_t kWideAcc = 2;                              // accumulators per CTA (256 columns each)
 constexpr uint32_t kWideStageBytes = 2 * kATileBytes + kATileBytes;  // A: 2 x 128 rows, B: 128-column half
-constexpr uint32_t kWideStagingBytes = 4 * 8192;              // per epilogue warp: 32 rows x 128 cols, 16-bit
+constexpr uint32_t kWideStagingPerWarp = 4096;                // 32 rows x 64 columns, 16-bit
 
 template <int EPI>
 struct WideShape {
   static constexpr int kStages = 4;
-  static constexpr uint32_t kStaging = EPI == EPI_FWD_STATS ? kWideStagingBytes : 0;
+  // The logits epilogue runs 8 warps, 4 per accumulator, so both accumulators drain at once; the
+  // store epilogue runs 4 warps that drain accumulator 0 and then accumulator 1.
+  static constexpr int kEpiWarps = EPI == EPI_FWD_STATS ? 8 : 4;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  static constexpr uint32_t kStaging = EPI == EPI_FWD_STATS ? kEpiWarps * kWideStagingPerWarp : 0;
   static constexpr uint32_t kBarBytes = (2 * kStages + 4) * 8 + 16;
   static constexpr uint32_t kSmemBytes = kStages * kWideStageBytes + kStaging + kBarBytes + 1024;
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
@@ -45,8 +49,8 @@ struct WideShape {
 
 // Logits epilogue of one 256-column accumulator for the warp's 32 rows (one row per lane): per
 // 128-column vocab tile the tile maximum, the exact label logit and the logits shifted by the maximum
-// (16-bit, through the warp's staging buffer and a TMA store). The TMEM loads of the second vocab tile
-// are issued before the first tile's shifted logits are staged and stored, so their latency overlaps.
+// (16-bit, staged in the warp's 4 KB shared-memory buffer 64 columns at a time and written with TMA
+// stores).
 template <typename WsT>
 __device__ __forceinline__ void wide_fwd_acc(const FwdEpiParams& p, const CUtensorMap* ws_map, bool write_ws,
                                              uint32_t tbase, uint32_t staging, int64_t row, int64_t y0,
@@ -60,15 +64,15 @@ __device__ __forceinline__ void wide_fwd_acc(const FwdEpiParams& p, const CUtens
   }
   const int tile0 = static_cast<int>(n0 / kVocabTile);
   const int ntiles = p.n_vtiles - tile0 < 2 ? p.n_vtiles - tile0 : 2;  // warp-uniform, >= 1
-  uint32_t r[4][32];
-#pragma unroll
-  for (int c = 0; c < 4; ++c) tmem_ld32_async(tbase + c * 32, r[c]);
 #pragma unroll 1
   for (int h = 0; h < ntiles; ++h) {
     const int64_t nh = n0 + h * kVocabTile;
     const int tile = tile0 + h;
     const int nvalid = static_cast<int>(p.vocab - nh < kVocabTile ? p.vocab - nh : kVocabTile);
     const int label_col = (label_local >= nh && label_local < nh + nvalid) ? static_cast<int>(label_local - nh) : -1;
+    uint32_t r[4][32];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) tmem_ld32_async(tbase + h * kVocabTile + c * 32, r[c]);
     tmem_wait_ld();
     float m = -CUDART_INF_F;
     if (nvalid == kVocabTile) {
@@ -97,37 +101,31 @@ __device__ __forceinline__ void wide_fwd_acc(const FwdEpiParams& p, const CUtens
           if (c * 32 + j == label_col) zy = __uint_as_float(r[c][j]);
       }
     }
-    // shifted logits packed two per register; the fp32 registers are then free for the next tile
-    uint32_t w[64];
-#pragma unroll
-    for (int c = 0; c < 4; ++c)
-#pragma unroll
-      for (int e = 0; e < 16; ++e)
-        w[c * 16 + e] = pack2<WsT>(__uint_as_float(r[c][2 * e]) - m, __uint_as_float(r[c][2 * e + 1]) - m);
-    if (h + 1 < ntiles) {
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32_async(tbase + kVocabTile + c * 32, r[c]);
-    }
-
     if (write_ws) {
-      // the previous TMA store of this warp must have read the staging buffer
-      if (lane == 0) bulk_wait_read_all();
-      __syncwarp();
-      // row `lane` of the two 64-column halves: 16-byte chunk q of a 128-byte row lands at q ^ (lane & 7)
 #pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        const uint32_t addr = staging + (q >> 3) * 4096u + static_cast<uint32_t>(lane) * 128u +
-                              ((static_cast<uint32_t>(q & 7) ^ static_cast<uint32_t>(lane & 7)) << 4);
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w[4 * q]), "r"(w[4 * q + 1]),
-                     "r"(w[4 * q + 2]), "r"(w[4 * q + 3])
-                     : "memory");
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        tma_store_2d(ws_map, staging, static_cast<int32_t>(nh), static_cast<int32_t>(y0));
-        tma_store_2d(ws_map, staging + 4096u, static_cast<int32_t>(nh + 64), static_cast<int32_t>(y0));
-        bulk_commit_group();
+      for (int hf = 0; hf < 2; ++hf) {
+        // the previous TMA store of this warp must have read the staging buffer
+        if (lane == 0) bulk_wait_read_all();
+        __syncwarp();
+        // row `lane`, 64 columns: 16-byte chunk q of the 128-byte row lands at q ^ (lane & 7)
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int c = hf * 2 + (q >> 2), e0 = (q & 3) * 8;
+          const uint32_t w0 = pack2<WsT>(__uint_as_float(r[c][e0]) - m, __uint_as_float(r[c][e0 + 1]) - m);
+          const uint32_t w1 = pack2<WsT>(__uint_as_float(r[c][e0 + 2]) - m, __uint_as_float(r[c][e0 + 3]) - m);
+          const uint32_t w2 = pack2<WsT>(__uint_as_float(r[c][e0 + 4]) - m, __uint_as_float(r[c][e0 + 5]) - m);
+          const uint32_t w3 = pack2<WsT>(__uint_as_float(r[c][e0 + 6]) - m, __uint_as_float(r[c][e0 + 7]) - m);
+          const uint32_t addr = staging + static_cast<uint32_t>(lane) * 128u +
+                                ((static_cast<uint32_t>(q) ^ static_cast<uint32_t>(lane & 7)) << 4);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w0), "r"(w1), "r"(w2), "r"(w3)
+                       : "memory");
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(ws_map, staging, static_cast<int32_t>(nh + hf * 64), static_cast<int32_t>(y0));
+          bulk_commit_group();
+        }
       }
     }
     if (row_ok) {
@@ -135,11 +133,10 @@ __device__ __forceinline__ void wide_fwd_acc(const FwdEpiParams& p, const CUtens
       if (label_col >= 0) p.label_logits[row * 2 + (student ? 0 : 1)] = zy;
     }
   }
-  tmem_wait_ld();  // no TMEM load of this warp stays in flight past the accumulator's release
 }
 
 template <bool A_MN, bool B_MN, int AMODE, bool TWO_SEG, int EPI, typename T16>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WideShape<EPI>::kThreads, 1)
     tc2w_gemm_kernel(const __grid_constant__ TcGemmParams p) {
   using S = WideShape<EPI>;
   constexpr uint32_t kIdesc = make_idesc_f16(std::is_same<T16, __nv_bfloat16>::value ? 1u : 0u, 256, kPairBN,
@@ -320,9 +317,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
+    // ------------------------------------------------------------ epilogue (warps 2.., both CTAs)
+    // TMEM lanes 32*(warp % 4) .. +31 belong to this warp; with 8 epilogue warps, warps 2..5 drain
+    // accumulator 0 and warps 6..9 accumulator 1
     const int quarter = warp & 3;
-    const uint32_t staging = staging_addr + static_cast<uint32_t>(quarter) * 8192u;
+    const int ew = warp - 2;
+    const int j_first = S::kEpiWarps == 8 ? (ew >> 2) : 0, j_last = S::kEpiWarps == 8 ? (ew >> 2) : 1;
+    const uint32_t staging = staging_addr + static_cast<uint32_t>(ew) * kWideStagingPerWarp;
     int it = 0;
     const bool prof = p.prof_slot >= 0 && warp == 2 && lane == 0;
     long long w_tfull = 0, busy = 0;
@@ -335,6 +336,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         tile_coords(t, p.m_tiles, p.n_tiles, p.group_m, mt0, nt0);
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
+          if (j < j_first || j > j_last) continue;
           const int64_t row = AMODE == A_INTERLEAVE
                                   ? static_cast<int64_t>(mt0) * 256 + j * 128 + rank * 64 + (quarter & 1) * 32 + lane
                                   : static_cast<int64_t>(mt0) * 512 + j * 256 + rank * 128 + quarter * 32 + lane;
@@ -350,7 +352,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       tile_coords(t, p.m_tiles, p.n_tiles, p.group_m, mt, nt);
       const int64_t n0 = static_cast<int64_t>(nt) * kPairBN;
 #pragma unroll 1
-      for (int j = 0; j < 2; ++j) {
+      for (int j = j_first; j <= j_last; ++j) {
         const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + j * kPairBN;
         if constexpr (EPI == EPI_FWD_STATS) {
           if constexpr (AMODE == A_INTERLEAVE) {

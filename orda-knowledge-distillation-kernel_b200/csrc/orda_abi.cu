@@ -259,7 +259,7 @@ int launch_tc2w(TcGemmParams& prm, int64_t M_tiles, int64_t N, cudaStream_t stre
   prm.prof_slot = gemm_profiling() ? (EPI == EPI_FWD_STATS ? 0 : (A_MN ? 2 : 1)) : -1;
   const int pairs = static_cast<int>(std::min<int64_t>(tiles, num_sms() / 2));
   count_launch();
-  k<<<2 * pairs, kGemmThreads, S::kSmemBytes, stream>>>(prm);
+  k<<<2 * pairs, S::kThreads, S::kSmemBytes, stream>>>(prm);
   return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
 }
 
