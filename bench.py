@@ -2,10 +2,10 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--divergence forward]
 
-Workload: N=8192 tokens (batch 4 x seq 2048), hidden 4096, vocab 128256, bf16,
+Workload (benchmark config 3): N=8192 tokens (batch 4 x seq 2048), hidden 4096, vocab 128256, bf16,
 tied teacher sharing the lm_head, forward KL at T=1 with weight 1.0, teacher CE weight 1.0 (the tied
 default), student hidden and lm_head take gradients, teacher hidden does not. Synthetic seeded inputs
-with BASELINE's distributions (hidden ~ N(0,1), lm_head ~ N(0, 0.02), 5% ignore_index labels).
+with the benchmark's distributions (hidden ~ N(0,1), lm_head ~ N(0, 0.02), 5% ignore_index labels).
 
 One step = ``distillation_loss(...)`` + ``loss.backward()``. ``value`` is whole-job tokens/s with the
 inputs resident in HBM (every input is larger than L2 or is re-read from HBM: the lm_head alone is
@@ -420,7 +420,7 @@ def run_ours(args):
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded; BASELINE config 3 distributions)",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded; benchmark config 3 distributions)",
             "config": {
                 "workload": "config 3: tied teacher at the Llama-3-8B head, N=8192 tokens/GPU (4x2048), H=4096, "
                             "V=128256, forward KL (T=1, weight 1), teacher CE 1.0, dHidden + dW",

@@ -237,7 +237,7 @@ def synthetic_case(
     w_std: float = 0.02,
     teacher_logit_std: float | None = None,
 ) -> dict:
-    """Seeded synthetic inputs with BASELINE.json's distributions (hidden ~ N(0,1), W ~ N(0, w_std),
+    """Seeded synthetic inputs with the benchmark configs' distributions (hidden ~ N(0,1), W ~ N(0, w_std),
     labels uniform with a fraction set to ignore_index, teacher logits ~ N(0, s) -> log_softmax)."""
     rng = np.random.default_rng(seed)
     out = {

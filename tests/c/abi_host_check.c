@@ -1,5 +1,5 @@
 /* Host-only check of the C ABI from plain C (no Python, no GPU): the header compiles as C, the
- * library links, the argument struct size matches, the workspace of the BASELINE config 3 shape is
+ * library links, the argument struct size matches, the workspace of the benchmark config 3 shape is
  * bounded, and invalid arguments are rejected before anything is launched. Built and run by
  * tests/test_c_abi.py with gcc. */
 #include <stdio.h>

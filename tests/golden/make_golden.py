@@ -10,7 +10,7 @@ Every case calls the reference's own PyTorch implementation, ``orda_ce_kernel.ap
 stored losses and gradients are the reference's outputs. Shapes, weights and seeds follow the
 reference's CPU correctness tests (``test/correctness/test_torch_backend_cpu.py``: seeds 101-106,
 weights 0.8/0.25/0.35, T=1.4/1.6/1.5/1.7, the all-ignored case) plus the small end of
-BASELINE config 1 (student-only CE) and config 2 (precomputed fp32 log-softmax teacher, T=2).
+benchmark config 1 (student-only CE) and config 2 (precomputed fp32 log-softmax teacher, T=2).
 """
 from __future__ import annotations
 
@@ -24,8 +24,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 
 def _import_reference():
-    for cand in (os.environ.get("ORDA_REFERENCE_SRC"), "/root/reference/src",
-                 os.path.join(HERE, "..", "..", "baseline", "_ref")):
+    # the reference package: its source tree (ORDA_REFERENCE_SRC) or the copy installed in baseline/_ref
+    for cand in (os.environ.get("ORDA_REFERENCE_SRC"), os.path.join(HERE, "..", "..", "baseline", "_ref")):
         if cand and os.path.isdir(os.path.join(cand, "orda_ce_kernel")):
             sys.path.insert(0, cand)
             break

@@ -3,7 +3,7 @@
 Cases follow the reference's GPU tests (test/correctness/test_public_api_cuda.py: fp16, BT=16,
 H=32 / Ht=48, V=257, chunk_size=7, kl 0.35, T=1.4, 5 teacher modes, mean/sum, kl=0, T=1,
 non-contiguous inputs, tied teacher_ce=0) with the reference's tolerances (loss 5e-3, grads 5e-2),
-plus every divergence variant and BASELINE-shaped slices in bf16 at the target tolerances
+plus every divergence variant and benchmark-shaped slices in bf16 at the target tolerances
 (loss 1e-3 relative, gradients 2e-2 relative) and fp32 at 1e-5.
 """
 from __future__ import annotations
@@ -239,7 +239,7 @@ VARIANTS = [("forward", 0.5), ("reverse", 0.5), ("jsd", 0.5), ("jsd", 0.2), ("js
 
 
 def _llm_inputs(mode, seed, BT=300, H=256, Ht=384, V=3000):
-    """BASELINE-style distributions: hidden ~ N(0,1), lm_head ~ N(0, 0.02), labels with ignored rows."""
+    """Benchmark-style distributions: hidden ~ N(0,1), lm_head ~ N(0, 0.02), labels with ignored rows."""
     return _make(mode, dtype=torch.bfloat16, seed=seed, BT=BT, H=H, Ht=Ht, V=V, scale=1.0, w_scale=0.02,
                  ignore_every=20)
 
@@ -250,7 +250,7 @@ def _llm_inputs(mode, seed, BT=300, H=256, Ht=384, V=3000):
 def test_divergence_variants_bf16(mode, div, beta, temperature):
     hs, weight, labels, teacher, tce, kw = _llm_inputs(mode, seed=11)
     if mode == "precomputed-logits":
-        # teacher logits ~ N(0, 2) given as fp32 log-softmax
+        # teacher logits ~ N(0, 2) given as fp32 log-softmax (benchmark config 2)
         g = torch.Generator().manual_seed(12)
         tl = torch.log_softmax(torch.randn(*labels.shape, weight.shape[0], generator=g) * 2.0, -1).cuda()
         teacher = PrecomputedTeacher(logits=tl)
@@ -269,7 +269,7 @@ def test_divergence_variants_bf16(mode, div, beta, temperature):
         assert _rel_err(teacher.weight.grad, ref.d_teacher_weight) < 2e-2
 
 
-# ----------------------------------------------------------------- BASELINE config 1 (fp32, full size)
+# ----------------------------------------------------------------- benchmark config 1 (fp32, full size)
 def test_config1_fp32_student_only():
     from oracle.distill_oracle import synthetic_case
 
@@ -370,7 +370,7 @@ def test_module_matches_functional_and_repeat_is_deterministic():
         assert float(x) == float(y)
 
 
-# ----------------------------------------------------------------- BASELINE-shaped slices (bf16)
+# ----------------------------------------------------------------- benchmark-shaped slices (bf16)
 def test_config2_precomputed_slice():
     from oracle.distill_oracle import synthetic_case
 
@@ -391,7 +391,7 @@ def test_config2_precomputed_slice():
 
 @pytest.mark.parametrize("div", ["forward", "reverse", "jsd"])
 def test_config3_llama_shape_slice(div):
-    """Llama-3-8B head (H=4096, V=128256), tied teacher, 64-row slice of BASELINE config 3."""
+    """Llama-3-8B head (H=4096, V=128256), tied teacher, 64-row slice of benchmark config 3."""
     from oracle.distill_oracle import synthetic_case
 
     c = synthetic_case(n=64, h=4096, v=128256, seed=3, ignore_frac=0.05)
