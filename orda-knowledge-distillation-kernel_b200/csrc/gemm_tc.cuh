@@ -41,6 +41,11 @@ struct TcGemmParams {
   int32_t m_tiles, n_tiles;
   int32_t kb0, kb1;  // k blocks of segment 0 / 1
   int32_t group_m;
+  // k split (wide kernel, single segment): unit t covers output tile t % (m_tiles*n_tiles) over k
+  // blocks [ks*kb_split, (ks+1)*kb_split) with ks = t / (m_tiles*n_tiles), and stores its fp32
+  // partial at st.out + ks * split_bytes. ksplit <= 1: no split.
+  int32_t ksplit, kb_split;
+  int64_t split_bytes;
   int32_t prof_slot;  // >= 0: accumulate pipeline wait counters into g_tc2_prof[prof_slot] (testing hook)
   int32_t* status;
   FwdEpiParams fwd;

@@ -159,8 +159,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WideShape<EPI>::kThr
   const int lane = threadIdx.x % 32;
   const uint32_t rank = cluster_ctarank();
   const int32_t pair = blockIdx.x / 2, npairs = gridDim.x / 2;
-  const int32_t num_tiles = p.m_tiles * p.n_tiles;
+  const int32_t mn_tiles = p.m_tiles * p.n_tiles;
+  const int32_t ks_n = p.ksplit > 1 ? p.ksplit : 1;
+  const int32_t num_tiles = mn_tiles * ks_n;
   const int32_t kb_total = TWO_SEG ? p.kb0 + p.kb1 : p.kb0;
+  // work unit t -> output tile (mt, nt), k split ks, k blocks [kb_begin, kb_begin + kb_count)
+  auto decode = [&](int32_t t, int32_t& mt, int32_t& nt, int32_t& ks, int32_t& kb_begin, int32_t& kb_count) {
+    ks = t / mn_tiles;
+    tile_coords(t - ks * mn_tiles, p.m_tiles, p.n_tiles, p.group_m, mt, nt);
+    kb_begin = ks_n > 1 ? ks * p.kb_split : 0;
+    kb_count = ks_n > 1 ? (kb_total - kb_begin < p.kb_split ? kb_total - kb_begin : p.kb_split) : kb_total;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S::kStages; ++s) {
@@ -195,10 +204,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WideShape<EPI>::kThr
       const bool prof = p.prof_slot >= 0;
       long long w_empty = 0, t_start = prof ? clk() : 0;
       for (int32_t t = pair; t < num_tiles && ok; t += npairs) {
-        int32_t mt, nt;
-        tile_coords(t, p.m_tiles, p.n_tiles, p.group_m, mt, nt);
+        int32_t mt, nt, ks, kb_begin, kb_count;
+        decode(t, mt, nt, ks, kb_begin, kb_count);
         const int32_t n_cta = nt * kPairBN + static_cast<int32_t>(rank) * 128;
-        for (int32_t kb = 0; kb < kb_total; ++kb) {
+        for (int32_t kbl = 0; kbl < kb_count; ++kbl) {
+          const int32_t kb = kb_begin + kbl;
           const long long c0 = prof ? clk() : 0;
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.status)) { ok = false; break; }
           if (prof) w_empty += clk() - c0;
@@ -252,10 +262,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WideShape<EPI>::kThr
       long long w_acc = 0, w_full = 0, t_start = prof ? clk() : 0;
       for (int32_t t = pair; t < num_tiles && ok; t += npairs, ++it) {
         const uint32_t bphase = static_cast<uint32_t>(it & 1);
+        int32_t mt_u, nt_u, ks_u, kb_begin_u, kb_count;
+        decode(t, mt_u, nt_u, ks_u, kb_begin_u, kb_count);
+        (void)mt_u; (void)nt_u; (void)ks_u; (void)kb_begin_u;
         // Head of the tile: the first `nhead` stages feed accumulator 0 as soon as the epilogue has
         // drained it, while the epilogue still drains accumulator 1; then the same stages feed
         // accumulator 1. After the head both accumulators advance together stage by stage.
-        const int32_t nhead = kb_total < S::kStages ? kb_total : S::kStages;
+        const int32_t nhead = kb_count < S::kStages ? kb_count : S::kStages;
         const int stage0 = stage;
         long long c0 = prof ? clk() : 0;
         if (!mbar_wait_cluster(tempty_bar(0), bphase ^ 1u, p.status)) { ok = false; break; }
@@ -287,7 +300,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WideShape<EPI>::kThr
                             operand_desc<B_MN>(sa + 2 * kATileBytes, kk), kIdesc, (kb | kk) != 0);
           tc_commit_pair_mc(empty_bar(hs), 3);
         }
-        for (int32_t kb = nhead; kb < kb_total; ++kb) {
+        for (int32_t kb = nhead; kb < kb_count; ++kb) {
           if (prof) c0 = clk();
           // the stage's bytes of both CTAs complete on this CTA's barrier: a CTA-scope wait suffices
           if (!mbar_wait(full_bar(stage), phase, p.status)) { ok = false; break; }
@@ -332,8 +345,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WideShape<EPI>::kThr
       // labels of this lane's two rows, loaded before the wait so their latency is hidden
       int64_t lab[2] = {0, 0};
       if constexpr (EPI == EPI_FWD_STATS) {
-        int32_t mt0, nt0;
-        tile_coords(t, p.m_tiles, p.n_tiles, p.group_m, mt0, nt0);
+        int32_t mt0, nt0, ks0, kbb0, kbc0;
+        decode(t, mt0, nt0, ks0, kbb0, kbc0);
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
           if (j < j_first || j > j_last) continue;
@@ -348,8 +361,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WideShape<EPI>::kThr
       const long long c1 = prof ? clk() : 0;
       if (prof) w_tfull += c1 - c0;
       tc_fence_after();
-      int32_t mt, nt;
-      tile_coords(t, p.m_tiles, p.n_tiles, p.group_m, mt, nt);
+      int32_t mt, nt, ks, kbb, kbc;
+      decode(t, mt, nt, ks, kbb, kbc);
       const int64_t n0 = static_cast<int64_t>(nt) * kPairBN;
 #pragma unroll 1
       for (int j = j_first; j <= j_last; ++j) {
@@ -370,7 +383,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WideShape<EPI>::kThr
           }
         } else {
           const int64_t row = static_cast<int64_t>(mt) * 512 + j * 256 + rank * 128 + quarter * 32 + lane;
-          store_epilogue<T16>(p.st, tbase, row, n0, kPairBN);
+          StoreEpiParams st = p.st;
+          if (ks_n > 1) st.out = static_cast<uint8_t*>(st.out) + ks * p.split_bytes;
+          store_epilogue<T16>(st, tbase, row, n0, kPairBN);
         }
         tc_fence_before();
         __syncwarp();

@@ -103,6 +103,7 @@ struct Plan {
   int32_t parts;       // column parts of the row sweeps
   int64_t part_cols;
   size_t off_part_records;
+  size_t off_dh_split;  // fp32 partials of the k-split dHidden GEMM: [2][C][max(H, Ht)]
 };
 
 int check_args(const orda_distill_args_t* a) {
@@ -182,6 +183,9 @@ Plan make_plan(const orda_distill_args_t* a, int64_t chunk_override) {
   p.part_cols = cdiv(cdiv(a->vocab, p.parts), 256) * 256;
   p.off_part_records = off;
   if (p.parts > 1) off = align256(off + sizeof(float) * kRowStats * p.parts * p.C);
+  p.off_dh_split = off;
+  if (a->compute_dtype != ORDA_F32 && (a->need_grad_student_hidden || a->need_grad_teacher_hidden))
+    off = align256(off + sizeof(float) * 2 * p.C * std::max(a->hidden, a->teacher_hidden));
   // the fp32 path materialises raw logits, so it always needs the student (and teacher) buffer
   const bool need_s = p.write_ws_s || a->compute_dtype == ORDA_F32;
   const bool need_t = p.teacher_acc && (p.write_ws_t || a->compute_dtype == ORDA_F32);
@@ -246,18 +250,20 @@ int launch_tc2(TcGemmParams& prm, int64_t M_tiles, int64_t N, cudaStream_t strea
 
 // Wide pair kernel (512 x 256 tiles); M_tiles counts 512-row (A_PLAIN) or 256-token (A_INTERLEAVE) tiles.
 template <bool A_MN, bool B_MN, int AMODE, bool TWO_SEG, int EPI, typename T16>
-int launch_tc2w(TcGemmParams& prm, int64_t M_tiles, int64_t N, cudaStream_t stream, int group_m) {
+int launch_tc2w(TcGemmParams& prm, int64_t M_tiles, int64_t N, cudaStream_t stream, int group_m,
+                int reserve_sms = 0) {
   using S = WideShape<EPI>;
   prm.m_tiles = static_cast<int32_t>(M_tiles);
   prm.n_tiles = static_cast<int32_t>(cdiv(N, kPairBN));
   prm.group_m = group_m;
-  const int64_t tiles = (int64_t)prm.m_tiles * prm.n_tiles;
+  const int64_t tiles = (int64_t)prm.m_tiles * prm.n_tiles * std::max<int32_t>(1, prm.ksplit);
   if (tiles <= 0) return ORDA_OK;
   if (tiles > INT32_MAX) return ORDA_ERR_UNSUPPORTED;
   auto k = tc2w_gemm_kernel<A_MN, B_MN, AMODE, TWO_SEG, EPI, T16>;
   set_smem(k, S::kSmemBytes);
   prm.prof_slot = gemm_profiling() ? (EPI == EPI_FWD_STATS ? 0 : (A_MN ? 2 : 1)) : -1;
-  const int pairs = static_cast<int>(std::min<int64_t>(tiles, num_sms() / 2));
+  const int usable = std::max(2, num_sms() - std::max(0, reserve_sms));
+  const int pairs = static_cast<int>(std::min<int64_t>(tiles, usable / 2));
   count_launch();
   k<<<2 * pairs, S::kThreads, S::kSmemBytes, stream>>>(prm);
   return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
@@ -362,9 +368,12 @@ int forward_tc(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const C
 }
 
 // dH[rows, N] = dZ[rows, V] * Wm[V, N]
+// dHidden has few output tiles (rows x H), so the wide pair kernel splits K (the vocabulary) in two:
+// each half accumulates an fp32 partial in the workspace and a sum kernel writes the 16-bit result.
+// The split does not depend on the row count, so chunking leaves every row's arithmetic unchanged.
 template <typename T16>
-int dh_tc(const orda_distill_args_t* a, const Plan& P, const void* dz, const void* wmat, int64_t ldw, int64_t n,
-          void* out, int64_t rows, int32_t* status, cudaStream_t s) {
+int dh_tc(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const void* dz, const void* wmat, int64_t ldw,
+          int64_t n, void* out, int64_t rows, int32_t* status, cudaStream_t s) {
   const int reserve = a->dweight_first ? a->overlap_reserve_sms : 0;
   TcGemmParams prm{};
   prm.status = status;
@@ -372,8 +381,22 @@ int dh_tc(const orda_distill_args_t* a, const Plan& P, const void* dz, const voi
   if ((rc = make_operand_map(&prm.a0, a->compute_dtype, dz, false, rows, a->vocab, P.vpad, kTileRows))) return rc;
   if ((rc = make_operand_map(&prm.b0, a->compute_dtype, wmat, true, n, a->vocab, ldw, 128))) return rc;
   prm.kb0 = static_cast<int32_t>(cdiv(a->vocab, kBK));
-  prm.st = StoreEpiParams{out, n, rows, n, 0, 0};
-  return launch_tc2<false, true, A_PLAIN, false, EPI_STORE, T16>(prm, cdiv(rows, 256), n, s, 8, reserve);
+  if (prm.kb0 < 2 || n % 8 != 0) {
+    prm.st = StoreEpiParams{out, n, rows, n, 0, 0};
+    return launch_tc2<false, true, A_PLAIN, false, EPI_STORE, T16>(prm, cdiv(rows, 256), n, s, 8, reserve);
+  }
+  float* part = reinterpret_cast<float*>(ws + P.off_dh_split);
+  prm.ksplit = 2;
+  prm.kb_split = static_cast<int32_t>(cdiv(prm.kb0, 2));
+  prm.split_bytes = static_cast<int64_t>(sizeof(float)) * rows * n;
+  prm.st = StoreEpiParams{part, n, rows, n, 1, 0};
+  if ((rc = launch_tc2w<false, true, A_PLAIN, false, EPI_STORE, T16>(prm, cdiv(rows, 512), n, s, 4, reserve)))
+    return rc;
+  const int64_t count8 = rows * n / 8;
+  count_launch();
+  sum_split_kernel<T16><<<static_cast<int>(std::min<int64_t>(cdiv(count8, 256), 4 * 148)), 256, 0, s>>>(
+      part, part + rows * n, static_cast<T16*>(out), count8);
+  return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
 }
 
 // dW[V, N] (+)= dZ0^T H0 (+ dZ1^T H1)
@@ -516,11 +539,11 @@ int grad_gemms(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const C
       int r = ORDA_OK;
       if (pm) pm->mark(ORDA_PHASE_DHIDDEN, 0);
       if (a->need_grad_student_hidden)
-        if ((r = dh_tc<WsT>(a, P, ws_s, a->weight, a->ld_weight, a->hidden, c.grad_hs, c.rows, st, s))) return r;
+        if ((r = dh_tc<WsT>(a, P, ws, ws_s, a->weight, a->ld_weight, a->hidden, c.grad_hs, c.rows, st, s))) return r;
       if (P.grad_t && a->need_grad_teacher_hidden) {
         const void* wm = tied ? a->weight : a->teacher_weight;
         const int64_t ldm = tied ? a->ld_weight : a->ld_teacher_weight;
-        if ((r = dh_tc<WsT>(a, P, ws_t, wm, ldm, a->teacher_hidden, c.grad_ht, c.rows, st, s))) return r;
+        if ((r = dh_tc<WsT>(a, P, ws, ws_t, wm, ldm, a->teacher_hidden, c.grad_ht, c.rows, st, s))) return r;
       }
       if (pm) pm->mark(ORDA_PHASE_DHIDDEN, 1);
       return r;

@@ -689,6 +689,22 @@ __global__ void mean_scale_kernel(const int64_t* labels, int64_t n, int64_t igno
   }
 }
 
+// out[r][c] = p0[r][c] + p1[r][c] (fp32 k-split partials of a GEMM, rows x n contiguous) in the 16-bit
+// output type; n is a multiple of 8.
+template <typename T>
+__global__ void sum_split_kernel(const float* p0, const float* p1, T* out, int64_t count8) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count8; i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 a0 = reinterpret_cast<const float4*>(p0)[2 * i], a1 = reinterpret_cast<const float4*>(p0)[2 * i + 1];
+    const float4 b0 = reinterpret_cast<const float4*>(p1)[2 * i], b1 = reinterpret_cast<const float4*>(p1)[2 * i + 1];
+    uint4 u;
+    u.x = pack2<T>(a0.x + b0.x, a0.y + b0.y);
+    u.y = pack2<T>(a0.z + b0.z, a0.w + b0.w);
+    u.z = pack2<T>(a1.x + b1.x, a1.y + b1.y);
+    u.w = pack2<T>(a1.z + b1.z, a1.w + b1.w);
+    reinterpret_cast<uint4*>(out)[i] = u;
+  }
+}
+
 // data *= *scale in place; every block returns at once when *scale == 1 (no memory traffic).
 template <typename T>
 __global__ void scale_grad_kernel(T* data, int64_t n, const float* scale) {
