@@ -70,10 +70,20 @@ def allreduce_weight_grad(weight: torch.Tensor, group=None, async_op: bool = Fal
 
 # ---------------------------------------------------------------------------------- vocab sharding
 class _NativeShardOps:
-    """The C-ABI phases of one vocab shard (include/orda_b200.h, orda_shard_*)."""
+    """The C-ABI phases of one vocab shard (include/orda_b200.h, orda_shard_*). The sharded Function
+    only talks to this interface (prepare / forward / merge / jsd_partials / backward / rescale), so the
+    CPU tests can run its collective choreography on gloo ranks with a torch restatement."""
 
     def __init__(self):
         self.lib = _native.load()
+
+    @staticmethod
+    def prepare(*args, **kwargs):
+        return prepare_call(*args, **kwargs)
+
+    @staticmethod
+    def rescale(ctx, grads, grad_output):
+        return rescale_saved_grads(ctx, grads, grad_output)
 
     def forward(self, pr):
         lib = self.lib
@@ -105,18 +115,29 @@ class _NativeShardOps:
                       "orda_shard_backward")
 
 
+def _all_gather_records(local: torch.Tensor, world: int, group) -> torch.Tensor:
+    """[world, n, ROW_STATS] gather of every rank's row records (one collective on NCCL; the list form
+    on backends without the single-tensor gather)."""
+    if dist.get_backend(group) == "nccl":
+        gathered = torch.empty((world, *local.shape), dtype=local.dtype, device=local.device)
+        dist.all_gather_into_tensor(gathered, local, group=group)
+        return gathered
+    parts = [torch.empty_like(local) for _ in range(world)]
+    dist.all_gather(parts, local, group=group)
+    return torch.stack(parts)
+
+
 class _VocabShardFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, student_hidden, teacher_hidden, weight, teacher_weight, labels, teacher_logits, spec,
-                vocab_offset, vocab_total, group):
+                vocab_offset, vocab_total, group, ops_factory):
         world = dist.get_world_size(group)
-        pr = prepare_call(student_hidden, teacher_hidden, weight, teacher_weight, labels, teacher_logits, spec,
-                          vocab_offset=vocab_offset, vocab_total=vocab_total)
-        ops = _NativeShardOps()
+        ops = ops_factory()
+        pr = ops.prepare(student_hidden, teacher_hidden, weight, teacher_weight, labels, teacher_logits, spec,
+                         vocab_offset=vocab_offset, vocab_total=vocab_total)
         n = pr.args.n_rows
         local = ops.forward(pr)
-        gathered = torch.empty((world, n, _native.ROW_STATS), dtype=torch.float32, device=pr.dev)
-        dist.all_gather_into_tensor(gathered, local, group=group)
+        gathered = _all_gather_records(local, world, group)
         row_stats = ops.merge(gathered, world, n)
         row_sums = None
         jsd = spec.kl_weight != 0.0 and spec.divergence == "jsd" and 0.0 < spec.jsd_beta < 1.0
@@ -132,6 +153,7 @@ class _VocabShardFunction(torch.autograd.Function):
         loss = out[_native.OUT_LOSS].clone()
         ce_s, ce_t, kl = (out[i].clone() for i in (_native.OUT_STUDENT_CE, _native.OUT_TEACHER_CE, _native.OUT_KL))
         ctx.save_for_backward(pr.g_hs, pr.g_ht, pr.g_w, pr.g_wt, out[_native.OUT_MEAN_SCALE].clone())
+        ctx.ops = ops
         ctx.shapes = (student_hidden.shape[1], pr.h_t)
         ctx.dtypes = (student_hidden.dtype, teacher_hidden.dtype if teacher_hidden is not None else None,
                       weight.dtype, teacher_weight.dtype if teacher_weight is not None else None)
@@ -143,12 +165,12 @@ class _VocabShardFunction(torch.autograd.Function):
     def backward(ctx, grad_output, *_):
         g_hs, g_ht, g_w, g_wt, _mean_scale = ctx.saved_tensors
         if grad_output is None:
-            return (None,) * 10
+            return (None,) * 11
         h, h_t = ctx.shapes
         dt_hs, dt_ht, dt_w, dt_wt = ctx.dtypes
-        r = rescale_saved_grads(ctx, [(g_hs, h, dt_hs), (g_ht, h_t, dt_ht), (g_w, h, dt_w), (g_wt, h_t, dt_wt)],
-                                grad_output)
-        return (r[0], r[1], r[2], r[3], None, None, None, None, None, None)
+        r = ctx.ops.rescale(ctx, [(g_hs, h, dt_hs), (g_ht, h_t, dt_ht), (g_w, h, dt_w), (g_wt, h_t, dt_wt)],
+                            grad_output)
+        return (r[0], r[1], r[2], r[3], None, None, None, None, None, None, None)
 
 
 def vocab_parallel_distillation_loss(student_hidden, weight_shard, labels, teacher, *, vocab_offset: int,
@@ -156,14 +178,16 @@ def vocab_parallel_distillation_loss(student_hidden, weight_shard, labels, teach
                                      teacher_ce_weight: float | None = None, kl_weight: float = 0.0,
                                      kl_temperature: float = 1.0, ignore_index: int = -100, reduction: str = "mean",
                                      kl_divergence: str = "forward", jsd_beta: float = 0.5,
-                                     fp32_grad_weight_accumulation: bool = False) -> DistillationLossOutput:
+                                     fp32_grad_weight_accumulation: bool = False,
+                                     _shard_ops=None) -> DistillationLossOutput:
     """``distillation_loss`` with the lm_head split by vocabulary rows across the ranks of ``group``.
 
     ``weight_shard`` holds vocab ids ``[vocab_offset, vocab_offset + weight_shard.shape[0])`` of a
     ``vocab_total``-row lm_head; a ``SeparateTeacher`` carries the same slice of the teacher lm_head and a
     ``PrecomputedTeacher(logits=...)`` the same columns of the teacher logits. Every rank passes all rows
     and the same labels (global vocab ids). Returns the global loss (identical on every rank); the
-    gradient of ``weight_shard`` is the complete gradient of that slice.
+    gradient of ``weight_shard`` is the complete gradient of that slice. ``_shard_ops`` replaces the
+    per-shard library phases (tests run the collectives on CPU ranks with a torch restatement).
     """
     if reduction not in ("mean", "sum"):
         raise ValueError(f"reduction must be 'mean' or 'sum', got {reduction!r}")
@@ -185,5 +209,5 @@ def vocab_parallel_distillation_loss(student_hidden, weight_shard, labels, teach
     if isinstance(teacher, (TiedTeacher, SeparateTeacher, PrecomputedTeacher)) is False:
         raise TypeError("teacher must be TiedTeacher, SeparateTeacher, or PrecomputedTeacher")
     out = _VocabShardFunction.apply(student_hidden, th, weight_shard, tw, labels, tl, spec, int(vocab_offset),
-                                    int(vocab_total), group)
+                                    int(vocab_total), group, _shard_ops or _NativeShardOps)
     return DistillationLossOutput(*out)

@@ -73,3 +73,173 @@ def test_token_parallel_matches_single_process():
         torch.testing.assert_close(ghs, a.grad[rows], rtol=1e-6, atol=1e-12)
         torch.testing.assert_close(ght, b.grad[rows], rtol=1e-6, atol=1e-12)
         torch.testing.assert_close(gw, c.grad, rtol=1e-6, atol=1e-12)
+
+
+# ------------------------------------------------------------------------------ vocab sharding on gloo
+class _Pr:
+    pass
+
+
+class _TorchShardOps:
+    """Torch (float64) restatement of the per-shard library phases for a tied teacher with CE and
+    forward / reverse KL: the row-record layout and LSE merge of the C ABI (include/orda_b200.h,
+    orda_shard_forward / orda_merge_row_stats / orda_shard_backward). Lets the CPU ranks run the
+    collective choreography of ``vocab_parallel_distillation_loss``."""
+
+    def prepare(self, hs, ht, w, wt, labels, tl, spec, vocab_offset=0, vocab_total=None):
+        from orda_ce_kernel import _native
+
+        pr = _Pr()
+        pr.spec, pr.off, pr.vt, pr.labels = spec, vocab_offset, vocab_total, labels
+        pr.hs, pr.ht, pr.w = hs.detach(), ht.detach(), w.detach()
+        pr.zs, pr.zt = pr.hs @ pr.w.t(), pr.ht @ pr.w.t()
+        pr.args = _Pr()
+        pr.args.n_rows = hs.shape[0]
+        pr.dev = hs.device
+        pr.h_t = ht.shape[1]
+        pr.g_hs = torch.zeros_like(pr.hs) if hs.requires_grad else None
+        pr.g_ht = torch.zeros_like(pr.ht) if (ht.requires_grad and spec.teacher_ce_weight > 0) else None
+        pr.g_w = torch.zeros_like(pr.w) if w.requires_grad else None
+        pr.g_wt = None
+        pr.out = torch.zeros(_native.OUT_SLOTS, dtype=torch.float64)
+        return pr
+
+    def _label_col(self, pr):
+        local = pr.labels - pr.off
+        has = (pr.labels != pr.spec.ignore_index) & (local >= 0) & (local < pr.w.shape[0])
+        return local.clamp(0, pr.w.shape[0] - 1), has
+
+    def forward(self, pr):
+        it = 1.0 / pr.spec.kl_temperature
+        rev = pr.spec.divergence == "reverse"
+        ms, mt = pr.zs.max(-1).values, pr.zt.max(-1).values
+        es1, et1 = (pr.zs - ms[:, None]).exp(), (pr.zt - mt[:, None]).exp()
+        esT, etT = ((pr.zs - ms[:, None]) * it).exp(), ((pr.zt - mt[:, None]) * it).exp()
+        cross = (esT * (pr.zs - pr.zt) * it).sum(-1) if rev else (etT * (pr.zt - pr.zs) * it).sum(-1)
+        col, has = self._label_col(pr)
+        rec = torch.zeros(pr.zs.shape[0], 16, dtype=torch.float64)
+        rec[:, 0], rec[:, 1], rec[:, 2] = ms, es1.sum(-1), esT.sum(-1)
+        rec[:, 3], rec[:, 4], rec[:, 5] = mt, et1.sum(-1), etT.sum(-1)
+        rec[:, 6] = cross
+        rec[:, 7] = torch.where(has, pr.zs.gather(1, col[:, None])[:, 0], torch.zeros(()))
+        rec[:, 8] = torch.where(has, pr.zt.gather(1, col[:, None])[:, 0], torch.zeros(()))
+        rec[:, 9] = has.double()
+        rec[:, 10] = 0.0 if rev else 1.0
+        rec[:, 11] = it
+        return rec
+
+    def merge(self, gathered, world, n):
+        it = float(gathered[0, 0, 11])
+        cross_t = bool(gathered[0, 0, 10] != 0)
+        out = torch.zeros(n, 16, dtype=torch.float64)
+        for side, (im, i1, iT) in enumerate(((0, 1, 2), (3, 4, 5))):
+            m = gathered[:, :, im].max(0).values
+            f1 = (gathered[:, :, im] - m).exp()
+            fT = ((gathered[:, :, im] - m) * it).exp()
+            out[:, im], out[:, i1], out[:, iT] = m, (gathered[:, :, i1] * f1).sum(0), (gathered[:, :, iT] * fT).sum(0)
+            if (side == 1) == cross_t:
+                out[:, 6] = (gathered[:, :, 6] * fT).sum(0)
+        out[:, 7] = (gathered[:, :, 7] * gathered[:, :, 9]).sum(0)
+        out[:, 8] = (gathered[:, :, 8] * gathered[:, :, 9]).sum(0)
+        out[:, 9] = gathered[:, :, 9].max(0).values
+        out[:, 10], out[:, 11] = gathered[0, :, 10], it
+        return out
+
+    def jsd_partials(self, pr, row_stats):  # pragma: no cover - JSD is not restated here
+        raise NotImplementedError
+
+    def backward(self, pr, rs, row_sums):
+        from orda_ce_kernel import _native
+
+        sp, T = pr.spec, pr.spec.kl_temperature
+        it = 1.0 / T
+        valid = pr.labels != sp.ignore_index
+        cnt = valid.sum().clamp(min=1).double()
+        scale = 1.0 / cnt if sp.reduction == "mean" else torch.ones((), dtype=torch.float64)
+        lse_s1, lse_t1 = rs[:, 0] + rs[:, 1].log(), rs[:, 3] + rs[:, 4].log()
+        lse_sT, lse_tT = rs[:, 0] * it + rs[:, 2].log(), rs[:, 3] * it + rs[:, 5].log()
+        ce_s, ce_t = (lse_s1 - rs[:, 7]) * valid, (lse_t1 - rs[:, 8]) * valid
+        rev = sp.divergence == "reverse"
+        div = (rs[:, 6] / (rs[:, 2] if rev else rs[:, 5]) + ((lse_tT - lse_sT) if rev else (lse_sT - lse_tT)))
+        div = div * T * T * valid
+        ps1, pt1 = (pr.zs - lse_s1[:, None]).exp(), (pr.zt - lse_t1[:, None]).exp()
+        lpsT, lptT = pr.zs * it - lse_sT[:, None], pr.zt * it - lse_tT[:, None]
+        psT, ptT = lpsT.exp(), lptT.exp()
+        col, has = self._label_col(pr)
+        onehot = torch.zeros_like(pr.zs).scatter_(1, col[:, None], 1.0) * has[:, None]
+        if rev:
+            # R = sum_v p_s (log p_s - log p_t) over the WHOLE vocabulary, from the merged record
+            a = lpsT - lptT
+            r = (rs[:, 6] / rs[:, 2] - lse_sT + lse_tT)[:, None]
+            dkl = psT * (a - r)
+        else:
+            dkl = psT - ptT
+        dzs = (sp.student_ce_weight * (ps1 - onehot) + sp.kl_weight * T * dkl) * valid[:, None] * scale
+        dzt = sp.teacher_ce_weight * (pt1 - onehot) * valid[:, None] * scale
+        if pr.g_hs is not None:
+            pr.g_hs.copy_(dzs @ pr.w)
+        if pr.g_ht is not None:
+            pr.g_ht.copy_(dzt @ pr.w)
+        if pr.g_w is not None:
+            pr.g_w.copy_(dzs.t() @ pr.hs + dzt.t() @ pr.ht)
+        s0, s1, s2 = ce_s.sum(), ce_t.sum(), div.sum()
+        o = pr.out
+        o[_native.OUT_STUDENT_CE], o[_native.OUT_TEACHER_CE], o[_native.OUT_KL] = s0 * scale, s1 * scale, s2 * scale
+        o[_native.OUT_LOSS] = (sp.student_ce_weight * s0 + sp.teacher_ce_weight * s1 + sp.kl_weight * s2) * scale
+        o[_native.OUT_MEAN_SCALE] = scale
+
+    @staticmethod
+    def rescale(ctx, grads, grad_output):
+        return [None if g is None else (g[:, :cols] * grad_output).to(dt) for g, cols, dt in grads]
+
+
+def _vocab_worker(rank, world, port, inputs, div, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from orda_ce_kernel.parallel import vocab_parallel_distillation_loss
+
+    hs0, ht0, w_all, labels = inputs
+    v = w_all.shape[0]
+    lo, hi = rank * v // world, (rank + 1) * v // world
+    hs = hs0.clone().requires_grad_(True)
+    ht = ht0.clone().requires_grad_(True)
+    w = w_all[lo:hi].clone().requires_grad_(True)
+    out = vocab_parallel_distillation_loss(hs, w, labels, TiedTeacher(ht), vocab_offset=lo, vocab_total=v,
+                                           kl_weight=0.4, kl_temperature=1.5, kl_divergence=div,
+                                           student_ce_weight=0.7, _shard_ops=_TorchShardOps)
+    (2.0 * out.loss).backward()
+    results[rank] = ((lo, hi), [float(x) for x in out], hs.grad.clone(), ht.grad.clone(), w.grad.clone())
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("div", ["forward", "reverse"])
+def test_vocab_parallel_matches_single_process(div):
+    """Two gloo ranks each holding half of the lm_head rows: the record gather + LSE merge, the
+    hidden-gradient all-reduce and the backward rescale reproduce the single-process loss and
+    gradients (oracle)."""
+    import numpy as np
+
+    from oracle.distill_oracle import distill_reference
+
+    g = torch.Generator().manual_seed(3)
+    n, h, v = 17, 6, 29
+    hs = torch.randn(n, h, generator=g, dtype=torch.float64)
+    ht = torch.randn(n, h, generator=g, dtype=torch.float64)
+    w = torch.randn(v, h, generator=g, dtype=torch.float64)
+    labels = torch.randint(0, v, (n,), generator=g)
+    labels[::5] = -100
+    with mp.Manager() as m:
+        results = m.dict()
+        mp.spawn(_vocab_worker, args=(2, 29655 if div == "forward" else 29656, (hs, ht, w, labels), div, results),
+                 nprocs=2, join=True)
+        results = dict(results)
+    ref = distill_reference(hs.numpy(), w.numpy(), labels.numpy(), mode="tied", teacher_hidden=ht.numpy(),
+                            student_ce_weight=0.7, kl_weight=0.4, kl_temperature=1.5, kl_divergence=div)
+    for rank in (0, 1):
+        (lo, hi), vals, ghs, ght, gw = results[rank]
+        exp = [ref.loss, ref.student_ce, ref.teacher_ce, ref.kl]
+        assert vals == pytest.approx([float(x) for x in exp], rel=1e-9, abs=1e-12)
+        np.testing.assert_allclose(ghs.numpy(), 2.0 * ref.d_student_hidden, rtol=1e-9, atol=1e-12)
+        np.testing.assert_allclose(ght.numpy(), 2.0 * ref.d_teacher_hidden, rtol=1e-9, atol=1e-12)
+        np.testing.assert_allclose(gw.numpy(), 2.0 * ref.d_weight[lo:hi], rtol=1e-9, atol=1e-12)
