@@ -424,11 +424,7 @@ __global__ void __launch_bounds__(256) jsd_sweep_kernel(RowParams p, float* row_
   const float beta = p.jsd_beta, lb = logf(beta), l1b = log1pf(-beta), it = p.inv_t;
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
-  const int64_t tasks = p.rows * p.parts;
-  for (int64_t task = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; task < tasks; task += warps) {
-    const int64_t row = task / p.parts;
-    int64_t c0, c1;
-    part_range(p, static_cast<int>(task - row * p.parts), c0, c1);
+  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; row < p.rows; row += warps) {
     const float2* tm = row_tile_maxima(p, row);
     const RowConsts c = row_consts(p, row);
     float acc_j = 0.f, acc_g = 0.f;
