@@ -145,8 +145,27 @@ class _TorchShardOps:
         out[:, 10], out[:, 11] = gathered[0, :, 10], it
         return out
 
-    def jsd_partials(self, pr, row_stats):  # pragma: no cover - JSD is not restated here
-        raise NotImplementedError
+    def _log_probs(self, pr, rs):
+        it = 1.0 / pr.spec.kl_temperature
+        lse_sT, lse_tT = rs[:, 0] * it + rs[:, 2].log(), rs[:, 3] * it + rs[:, 5].log()
+        return pr.zs * it - lse_sT[:, None], pr.zt * it - lse_tT[:, None]
+
+    def _jsd_terms(self, pr, rs):
+        b = pr.spec.jsd_beta
+        lps, lpt = self._log_probs(pr, rs)
+        lm = torch.logaddexp(torch.log(torch.tensor(b, dtype=torch.float64)) + lpt,
+                             torch.log1p(torch.tensor(-b, dtype=torch.float64)) + lps)
+        return lps, lpt, lm
+
+    def jsd_partials(self, pr, row_stats):
+        """This shard's [sum_v b p_t (log p_t - log m) + (1-b) p_s (log p_s - log m), sum_v p_s g]."""
+        b = pr.spec.jsd_beta
+        lps, lpt, lm = self._jsd_terms(pr, row_stats)
+        ps, pt = lps.exp(), lpt.exp()
+        valid = (pr.labels != pr.spec.ignore_index).double()
+        sj = (b * pt * (lpt - lm) + (1 - b) * ps * (lps - lm)).sum(-1) * valid
+        sg = (ps * (1 - b) * (lps - lm)).sum(-1) * valid
+        return torch.stack([sj, sg], -1)
 
     def backward(self, pr, rs, row_sums):
         from orda_ce_kernel import _native
@@ -160,14 +179,21 @@ class _TorchShardOps:
         lse_sT, lse_tT = rs[:, 0] * it + rs[:, 2].log(), rs[:, 3] * it + rs[:, 5].log()
         ce_s, ce_t = (lse_s1 - rs[:, 7]) * valid, (lse_t1 - rs[:, 8]) * valid
         rev = sp.divergence == "reverse"
-        div = (rs[:, 6] / (rs[:, 2] if rev else rs[:, 5]) + ((lse_tT - lse_sT) if rev else (lse_sT - lse_tT)))
-        div = div * T * T * valid
+        if sp.divergence == "jsd":
+            div = row_sums[:, 0] * T * T * valid
+        else:
+            div = (rs[:, 6] / (rs[:, 2] if rev else rs[:, 5]) + ((lse_tT - lse_sT) if rev else (lse_sT - lse_tT)))
+            div = div * T * T * valid
         ps1, pt1 = (pr.zs - lse_s1[:, None]).exp(), (pr.zt - lse_t1[:, None]).exp()
         lpsT, lptT = pr.zs * it - lse_sT[:, None], pr.zt * it - lse_tT[:, None]
         psT, ptT = lpsT.exp(), lptT.exp()
         col, has = self._label_col(pr)
         onehot = torch.zeros_like(pr.zs).scatter_(1, col[:, None], 1.0) * has[:, None]
-        if rev:
+        if sp.divergence == "jsd":
+            # g = (1 - b)(log p_s - log m); the row sum of p_s g comes all-reduced from jsd_partials
+            _, _, lm = self._jsd_terms(pr, rs)
+            dkl = psT * ((1 - sp.jsd_beta) * (lpsT - lm) - row_sums[:, 1:2])
+        elif rev:
             # R = sum_v p_s (log p_s - log p_t) over the WHOLE vocabulary, from the merged record
             a = lpsT - lptT
             r = (rs[:, 6] / rs[:, 2] - lse_sT + lse_tT)[:, None]
@@ -206,14 +232,14 @@ def _vocab_worker(rank, world, port, inputs, div, results):
     ht = ht0.clone().requires_grad_(True)
     w = w_all[lo:hi].clone().requires_grad_(True)
     out = vocab_parallel_distillation_loss(hs, w, labels, TiedTeacher(ht), vocab_offset=lo, vocab_total=v,
-                                           kl_weight=0.4, kl_temperature=1.5, kl_divergence=div,
+                                           kl_weight=0.4, kl_temperature=1.5, kl_divergence=div, jsd_beta=0.3,
                                            student_ce_weight=0.7, _shard_ops=_TorchShardOps)
     (2.0 * out.loss).backward()
     results[rank] = ((lo, hi), [float(x) for x in out], hs.grad.clone(), ht.grad.clone(), w.grad.clone())
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("div", ["forward", "reverse"])
+@pytest.mark.parametrize("div", ["forward", "reverse", "jsd"])
 def test_vocab_parallel_matches_single_process(div):
     """Two gloo ranks each holding half of the lm_head rows: the record gather + LSE merge, the
     hidden-gradient all-reduce and the backward rescale reproduce the single-process loss and
@@ -231,11 +257,12 @@ def test_vocab_parallel_matches_single_process(div):
     labels[::5] = -100
     with mp.Manager() as m:
         results = m.dict()
-        mp.spawn(_vocab_worker, args=(2, 29655 if div == "forward" else 29656, (hs, ht, w, labels), div, results),
-                 nprocs=2, join=True)
+        port = {"forward": 29655, "reverse": 29656, "jsd": 29657}[div]
+        mp.spawn(_vocab_worker, args=(2, port, (hs, ht, w, labels), div, results), nprocs=2, join=True)
         results = dict(results)
     ref = distill_reference(hs.numpy(), w.numpy(), labels.numpy(), mode="tied", teacher_hidden=ht.numpy(),
-                            student_ce_weight=0.7, kl_weight=0.4, kl_temperature=1.5, kl_divergence=div)
+                            student_ce_weight=0.7, kl_weight=0.4, kl_temperature=1.5, kl_divergence=div,
+                            jsd_beta=0.3)
     for rank in (0, 1):
         (lo, hi), vals, ghs, ght, gw = results[rank]
         exp = [ref.loss, ref.student_ce, ref.teacher_ce, ref.kl]
