@@ -16,7 +16,15 @@ NCCL, overlapped with the dHidden GEMM.
 
 ``--impl reference`` times the reference's own PyTorch CPU implementation
 (``distillation_loss(..., backend="torch")`` from the installed reference package) on a 256-row
-slice of the same workload using all host threads.
+slice of the same workload using every physical core of the host (the thread count is set
+explicitly, so it is the same under torchrun as in a plain run).
+
+Unless ``--no-extras`` is given, the JSON line also carries ``extra_workloads``: the other benchmark
+configurations measured in the same run, each with tokens/s, ms/step and its tensor-roofline
+fraction (one GPU: config 3 with reverse KL and JSD, config 2 with the precomputed fp32 teacher and
+its teacher-stream HBM GB/s, config 4 and config 5 with its precomputed variant; N GPUs: config 4
+with the lm_head split by vocabulary over the N ranks, its loss checked against one GPU, and config
+5 with its 65536 tokens split over the N ranks).
 """
 from __future__ import annotations
 
@@ -52,6 +60,8 @@ def _args():
     p.add_argument("--rows", type=int, default=N_TOK, help="tokens per GPU")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-extras", action="store_true", help="skip the extra_workloads measurements")
+    p.add_argument("--only-extras", default="", help="comma-separated extra workload keys to run (default: all)")
     p.add_argument("--reserve-sms", type=int, default=-1,
                    help="SMs the dHidden GEMM leaves to the overlapped dW all-reduce (N>1; -1: default)")
     return p.parse_args()
@@ -62,6 +72,37 @@ def _dist_env():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     return world, rank, local
+
+
+def _physical_cores() -> int:
+    """Physical cores this process may run on (hyper-threads do not add matmul throughput)."""
+    aff = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    try:
+        import psutil
+
+        phys = psutil.cpu_count(logical=False) or aff
+    except Exception:
+        phys = aff
+    return max(1, min(phys, aff))
+
+
+def _cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def _use_all_cores(torch) -> int:
+    """Sets torch's intra-op threads to the physical core count (torchrun exports OMP_NUM_THREADS=1,
+    which would otherwise leave the CPU reference on one core) and returns it."""
+    n = _physical_cores()
+    torch.set_num_threads(n)
+    return torch.get_num_threads()
 
 
 def _workload(torch, rows, seed_offset, device):
@@ -170,6 +211,7 @@ def _import_reference_package():
 
 def _cpu_reference_rows(torch, rows, divergence):
     """Times the reference's torch CPU path on `rows` rows of the workload; returns (tok/s, sample, kind)."""
+    _use_all_cores(torch)
     hs, ht, w, labels = _workload(torch, N_TOK, 0, None)
     hs, ht, labels = hs[:rows].clone(), ht[:rows].clone(), labels[:rows].clone()
     ref = _import_reference_package() if divergence == "forward" else None
@@ -207,13 +249,367 @@ def _cpu_reference_rows(torch, rows, divergence):
     return rows / t, f"{rows} of {N_TOK} rows, H={HID}, V={VOCAB}, bf16, median of 3", kind
 
 
+# ------------------------------------------------------------------------------------- extra workloads
+H5, V5, N5 = 4096, 128256, 65536                     # config 5 (long context)
+HS4, HT4, V4, N4 = 3584, 8192, 151936, 16384         # config 4 (separate teacher)
+H2, V2, N2 = 2048, 32000, 4096                       # config 2 (precomputed teacher)
+PRECOMP_CHUNK = 8192                                 # rows per library chunk of the config 5 precomputed run
+
+
+def _dev_gen(torch, dev, seed):
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    return g
+
+
+def _dev_randn(torch, shape, seed, dev, std=1.0, dtype=None):
+    t = torch.randn(shape, generator=_dev_gen(torch, dev, seed), device=dev, dtype=torch.float32)
+    if std != 1.0:
+        t.mul_(std)
+    return t.to(dtype or torch.bfloat16)
+
+
+def _dev_labels(torch, n, v, frac, seed, dev):
+    g = _dev_gen(torch, dev, seed)
+    lab = torch.randint(0, v, (n,), generator=g, device=dev)
+    return lab.masked_fill(torch.rand(n, generator=g, device=dev) < frac, -100)
+
+
+def _dev_teacher_logprobs(torch, rows, v, seed, dev, std=2.0, block=4096):
+    """fp32 log_softmax of N(0, std) teacher logits, generated block by block on the device."""
+    out = torch.empty((rows, v), dtype=torch.float32, device=dev)
+    for i, r0 in enumerate(range(0, rows, block)):
+        r1 = min(rows, r0 + block)
+        z = torch.randn((r1 - r0, v), generator=_dev_gen(torch, dev, seed + i), device=dev, dtype=torch.float32)
+        out[r0:r1] = torch.log_softmax(z * std, dim=-1)
+        del z
+    return out
+
+
+def _primed(ev):
+    # the library records these events through their raw handles; recording each once here makes torch
+    # create the underlying CUDA event (torch creates events lazily on first record)
+    ev.record()
+    return ev
+
+
+def _sync_all(torch, pg):
+    torch.cuda.synchronize()
+    if pg is not None:
+        import torch.distributed as dist
+
+        dist.barrier(group=pg)
+        torch.cuda.synchronize()
+
+
+def _max_over_ranks(torch, value, pg, dev):
+    if pg is None:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=pg)
+    return float(t.item())
+
+
+def _timed(torch, step, steps, warmup, pg, dev, phases):
+    """`warmup` untimed steps, then `steps` steps between two CUDA events (barrier + synchronize on both
+    sides); returns (ms per step as the max over ranks, mean phase ms of the library's last chunk)."""
+    from orda_ce_kernel import _native
+
+    for _ in range(warmup):
+        step(None)
+    _sync_all(torch, pg)
+    evs = [[_primed(torch.cuda.Event(enable_timing=True)) for _ in range(2 * _native.PHASES)]
+           for _ in range(steps)] if phases else None
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _sync_all(torch, pg)
+    start.record()
+    for i in range(steps):
+        step(evs[i] if evs else None)
+    end.record()
+    _sync_all(torch, pg)
+    ms = _max_over_ranks(torch, start.elapsed_time(end) / steps, pg, dev)
+    ph = None
+    if evs:
+        ph = [statistics.mean(evs[i][2 * p].elapsed_time(evs[i][2 * p + 1]) for i in range(steps))
+              for p in range(_native.PHASES)]
+    return ms, ph
+
+
+def _phase_dict(ph):
+    if ph is None:
+        return None
+    names = ("logits GEMM", "row kernels", "dHidden GEMM", "dWeight GEMM")
+    return {n: v for n, v in zip(names, ph)}
+
+
+def _roof(flops_tok, tokens_per_gpu, ms):
+    burst, sus, _, src = _peaks()
+    tf = flops_tok * tokens_per_gpu / (ms / 1e3) / 1e12
+    return {"tflops_per_gpu": tf, "frac_of_bf16_peak": tf / burst, "frac_of_sustained_bf16_peak": tf / sus,
+            "peak_source": src}
+
+
+def run_extras(args, torch, dev, pg, world, rank, reserve, main_inputs):
+    """The other benchmark configurations, measured in the same process after the headline run."""
+    import orda_ce_kernel as ok
+    from orda_ce_kernel import _fused
+
+    only = {k for k in args.only_extras.split(",") if k}
+    steps, warmup = max(2, min(args.steps, 10)), 3
+    results = []
+
+    def want(key):
+        return not only or key in only
+
+    def free():
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+
+    def dp_step(w, kw_fn, done):
+        """One token-sharded step (distillation_loss + backward; with N > 1 the lm_head gradient is
+        all-reduced on a comm stream beside the dHidden GEMM, like the headline run)."""
+        comm = torch.cuda.Stream(device=dev) if pg is not None else None
+
+        def step(evs):
+            w.grad = None
+            with _fused.instrument(phase_events=evs, dweight_done_event=done, dweight_first=pg is not None,
+                                   reserve_sms=reserve):
+                out = kw_fn()
+                out.loss.backward()
+            if pg is not None:
+                import torch.distributed as dist
+
+                comm.wait_event(done)
+                with torch.cuda.stream(comm):
+                    dist.all_reduce(w.grad, group=pg)
+                torch.cuda.current_stream().wait_stream(comm)
+            return out
+
+        return step
+
+    done = _primed(torch.cuda.Event()) if pg is not None else None
+
+    # ---- config 3, the other divergence variants (one GPU: a per-GPU property)
+    if world == 1:
+        hs, ht, w, labels = main_inputs
+        for div in ("reverse", "jsd"):
+            key = f"config3_{div}"
+            if not want(key):
+                continue
+
+            def call(div=div):
+                hs.grad = None
+                return ok.distillation_loss(hs, w, labels, ok.TiedTeacher(ht), kl_weight=1.0, kl_temperature=1.0,
+                                            kl_divergence=div, jsd_beta=0.5)
+
+            ms, ph = _timed(torch, dp_step(w, call, done), steps, warmup, pg, dev, True)
+            results.append({"key": key, "workload": f"config 3 with {div} KL" + (" (beta 0.5)" if div == "jsd" else "")
+                            + ": tied teacher, N=8192, H=4096, V=128256, T=1, teacher CE 1.0",
+                            "value": hs.shape[0] / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+                            **_roof(10.0 * HID * VOCAB, hs.shape[0], ms), "phase_ms": _phase_dict(ph),
+                            "parity": "unpinned by the reference (no reverse KL / JSD there); checked against "
+                                      "the in-repo float64 restatement"})
+        free()
+
+    # ---- config 2: precomputed fp32 teacher log-probs (one GPU)
+    if world == 1 and want("config2"):
+        hs2 = _dev_randn(torch, (N2, H2), 21, dev).requires_grad_(True)
+        w2 = _dev_randn(torch, (V2, H2), 22, dev, std=0.02).requires_grad_(True)
+        lab2 = _dev_labels(torch, N2, V2, 0.05, 23, dev)
+        tl2 = _dev_teacher_logprobs(torch, N2, V2, 24, dev)
+
+        def call2():
+            hs2.grad = None
+            return ok.distillation_loss(hs2, w2, lab2, ok.PrecomputedTeacher(logits=tl2), student_ce_weight=0.5,
+                                        kl_weight=0.5, kl_temperature=2.0)
+
+        ms, ph = _timed(torch, dp_step(w2, call2, done), steps, warmup, pg, dev, True)
+        results.append(_precomputed_line("config2", "config 2: precomputed fp32 teacher log-probs, N=4096, H=2048, "
+                                         "V=32000, forward KL T=2, CE 0.5 + KL 0.5", N2, N2, V2, H2, ms, ph,
+                                         "forward"))
+        del hs2, w2, lab2, tl2
+        free()
+
+    # ---- config 4: separate teacher; vocabulary split over the ranks
+    if want("config4"):
+        results.append(_config4(torch, ok, dev, pg, world, rank, steps, warmup))
+        free()
+
+    # ---- config 5: long context, tokens split over the ranks (strong scaling)
+    if want("config5"):
+        rows = N5 // world
+        r0 = rank * rows
+        hs5 = _dev_randn(torch, (N5, H5), 51, dev)[r0:r0 + rows].clone().requires_grad_(True)
+        ht5 = _dev_randn(torch, (N5, H5), 52, dev)[r0:r0 + rows].clone()
+        w5 = _dev_randn(torch, (V5, H5), 53, dev, std=0.02).requires_grad_(True)
+        lab5 = _dev_labels(torch, N5, V5, 0.05, 54, dev)[r0:r0 + rows].clone()
+
+        def call5():
+            hs5.grad = None
+            return ok.distillation_loss(hs5, w5, lab5, ok.TiedTeacher(ht5), kl_weight=1.0, kl_temperature=1.0,
+                                        kl_divergence="jsd", jsd_beta=0.5)
+
+        ms, ph = _timed(torch, dp_step(w5, call5, done), max(2, steps // 2), warmup, pg, dev, True)
+        results.append({"key": "config5", "workload": f"config 5: N=65536 (2x32768) split over {world} GPU(s) "
+                        f"({rows} tokens each), tied teacher, JSD beta=0.5, T=1, H=4096, V=128256",
+                        "value": N5 / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "scaling": "strong",
+                        "tokens_per_gpu": rows, **_roof(10.0 * H5 * V5, rows, ms), "phase_ms": _phase_dict(ph),
+                        "parallelism": f"token-sharded dp{world}" if world > 1 else "single GPU",
+                        "parity": "JSD unpinned by the reference; checked against the in-repo float64 restatement"})
+        del hs5, ht5, lab5
+        free()
+        if want("config5_precomputed"):
+            hs5 = _dev_randn(torch, (N5, H5), 51, dev)[r0:r0 + rows].clone().requires_grad_(True)
+            lab5 = _dev_labels(torch, N5, V5, 0.05, 54, dev)[r0:r0 + rows].clone()
+            tl5 = _dev_teacher_logprobs(torch, rows, V5, 5500 + 100 * rank, dev)
+            cfg = ok.KernelConfig(chunk_size=PRECOMP_CHUNK)
+
+            def call5p():
+                hs5.grad = None
+                return ok.distillation_loss(hs5, w5, lab5, ok.PrecomputedTeacher(logits=tl5), kl_weight=1.0,
+                                            kl_temperature=1.0, kl_divergence="jsd", jsd_beta=0.5, config=cfg)
+
+            ms, ph = _timed(torch, dp_step(w5, call5p, done), max(2, steps // 2), warmup, pg, dev, True)
+            line = _precomputed_line("config5_precomputed", f"config 5 precomputed variant: fp32 teacher log-probs "
+                                     f"(N(0,2) before log_softmax), N=65536 split over {world} GPU(s), JSD beta=0.5, "
+                                     f"T=1, H=4096, V=128256, {PRECOMP_CHUNK}-row chunks",
+                                     N5, rows, V5, H5, ms, ph, "jsd", last_chunk_rows=min(rows, PRECOMP_CHUNK))
+            line["scaling"] = "strong"
+            results.append(line)
+            del hs5, lab5, tl5
+        del w5
+        free()
+    return results
+
+
+def _row_phase_bytes(rows, vocab, divergence):
+    """Algorithmic HBM bytes of the row phase of a precomputed-teacher chunk: per (row, column) the
+    statistics pass reads the 16-bit student logits and the fp32 teacher log-prob, the dlogits sweep
+    reads both again and writes the 16-bit dlogits; JSD adds one more read of both."""
+    per = (2 + 4) + (2 + 4 + 2) + ((2 + 4) if divergence == "jsd" else 0)
+    passes = 3 if divergence == "jsd" else 2
+    return rows * vocab * per, rows * vocab * 4 * passes
+
+
+def _precomputed_line(key, workload, tokens_total, tokens_per_gpu, vocab, hidden, ms, ph, divergence,
+                      last_chunk_rows=None):
+    _, _, hbm, src = _peaks()
+    rows = last_chunk_rows or tokens_per_gpu
+    total_bytes, teacher_bytes = _row_phase_bytes(rows, vocab, divergence)
+    row_ms = ph[1] if ph else None
+    line = {"key": key, "workload": workload, "value": tokens_total / (ms / 1e3), "unit": "tokens/s",
+            "ms_per_step": ms, "tokens_per_gpu": tokens_per_gpu, **_roof(6.0 * hidden * vocab, tokens_per_gpu, ms),
+            "phase_ms": _phase_dict(ph)}
+    if row_ms:
+        line["teacher_stream"] = {
+            "what": "fp32 teacher log-probs streamed by the row kernels of one chunk "
+                    f"({rows} rows x {vocab} x 4 B per pass, {teacher_bytes // (rows * vocab * 4)} passes)",
+            "teacher_gbs": teacher_bytes / (row_ms / 1e3) / 1e9,
+            "row_phase_hbm_gbs": total_bytes / (row_ms / 1e3) / 1e9,
+            "row_phase_bytes": total_bytes, "row_phase_ms": row_ms,
+            "hbm_peak_gbs": hbm, "frac_of_hbm_peak": total_bytes / (row_ms / 1e3) / 1e9 / hbm, "peak_source": src}
+    return line
+
+
+def _config4(torch, ok, dev, pg, world, rank, steps, warmup):
+    """Config 4: separate teacher (Hs=3584, Ht=8192, V=151936, N=16384, 10% ignore, reverse KL T=1.5);
+    with N > 1 GPUs each rank holds V/N rows of both lm_heads (vocab sharding, strong scaling)."""
+    hs = _dev_randn(torch, (N4, HS4), 41, dev).requires_grad_(True)
+    ht = _dev_randn(torch, (N4, HT4), 42, dev)
+    w_full = _dev_randn(torch, (V4, HS4), 43, dev, std=0.02)
+    wt_full = _dev_randn(torch, (V4, HT4), 44, dev, std=0.02)
+    labels = _dev_labels(torch, N4, V4, 0.10, 45, dev)
+    kw = dict(kl_weight=1.0, kl_temperature=1.5, kl_divergence="reverse")
+    flops_tok = 2.0 * HT4 * V4 + 6.0 * HS4 * V4
+    line = {"key": "config4", "unit": "tokens/s", "scaling": "strong",
+            "parity": "reverse KL unpinned by the reference; checked against the in-repo float64 restatement"}
+    if pg is None:
+        w = w_full.requires_grad_(True)
+
+        def step(evs):
+            hs.grad = None
+            w.grad = None
+            from orda_ce_kernel import _fused
+
+            with _fused.instrument(phase_events=evs):
+                out = ok.distillation_loss(hs, w, labels, ok.SeparateTeacher(ht, wt_full), **kw)
+                out.loss.backward()
+            return out
+
+        ms, ph = _timed(torch, step, steps, warmup, None, dev, True)
+        line.update({"workload": "config 4: separate teacher, N=16384, Hs=3584, Ht=8192, V=151936, reverse KL "
+                                 "T=1.5, 10% ignore_index, one GPU", "value": N4 / (ms / 1e3), "ms_per_step": ms,
+                     **_roof(flops_tok, N4, ms), "phase_ms": _phase_dict(ph), "parallelism": "single GPU"})
+        del w
+        return line
+
+    import torch.distributed as dist
+
+    from orda_ce_kernel.parallel import vocab_parallel_distillation_loss
+
+    # the single-GPU loss of the same seeded inputs (rank 0), the per-N correctness check
+    single = None
+    if rank == 0:
+        with torch.no_grad():
+            single = float(ok.distillation_loss(hs.detach(), w_full, labels, ok.SeparateTeacher(ht, wt_full), **kw).loss)
+    lo, hi = rank * V4 // world, (rank + 1) * V4 // world
+    w = w_full[lo:hi].clone().requires_grad_(True)
+    wt = wt_full[lo:hi].clone()
+    del w_full, wt_full
+    torch.cuda.empty_cache()
+    last = {}
+
+    def step(evs):
+        hs.grad = None
+        w.grad = None
+        out = vocab_parallel_distillation_loss(hs, w, labels, ok.SeparateTeacher(ht, wt), vocab_offset=lo,
+                                               vocab_total=V4, group=pg, **kw)
+        out.loss.backward()
+        last["loss"] = out.loss
+        return out
+
+    ms, _ = _timed(torch, step, steps, warmup, pg, dev, False)
+    loss = float(last["loss"].detach())
+    # the two collectives of the sharded step, timed alone at the same sizes
+    coll = {}
+    t_dh = torch.empty((N4, HS4), dtype=torch.bfloat16, device=dev).normal_()
+    rec = torch.zeros((N4, 16), dtype=torch.float32, device=dev)
+    rec_all = torch.empty((world, N4, 16), dtype=torch.float32, device=dev)
+    for name, op, nbytes in (
+        ("dhidden_allreduce", lambda: dist.all_reduce(t_dh, group=pg), t_dh.numel() * 2),
+        ("row_record_allgather", lambda: dist.all_gather_into_tensor(rec_all, rec, group=pg), rec_all.numel() * 4),
+    ):
+        for _ in range(3):
+            op()
+        _sync_all(torch, pg)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(10):
+            op()
+        b.record()
+        _sync_all(torch, pg)
+        coll[name] = {"ms": _max_over_ranks(torch, a.elapsed_time(b) / 10, pg, dev), "bytes": nbytes}
+    del t_dh, rec, rec_all
+    line.update({"workload": f"config 4: separate teacher, N=16384, Hs=3584, Ht=8192, V=151936, reverse KL T=1.5, "
+                             f"10% ignore_index; lm_head and teacher lm_head split by vocabulary over {world} GPUs "
+                             f"({hi - lo} rows each), row records all-gathered (NCCL), dHidden all-reduced",
+                 "value": N4 / (ms / 1e3), "ms_per_step": ms, "parallelism": f"vocab-sharded vp{world}",
+                 **_roof(flops_tok / world, N4, ms), "collectives_alone": coll, "loss": loss})
+    if single is not None:
+        line["loss_single_gpu"] = single
+        line["loss_rel_diff_vs_single_gpu"] = abs(loss - single) / abs(single)
+    return line
+
+
 def run_reference(args):
     import torch
 
     world, rank, _ = _dist_env()
     if rank != 0:
         return 0
-    threads = torch.get_num_threads()
+    threads = _use_all_cores(torch)
     hs, ht, w, labels = _workload(torch, N_TOK, 0, None)
     hs, ht, labels = hs[:CPU_ROWS].clone(), ht[:CPU_ROWS].clone(), labels[:CPU_ROWS].clone()
     ref = _import_reference_package()
@@ -243,6 +639,7 @@ def run_reference(args):
                    "tokens": CPU_ROWS, "hidden": HID, "vocab": VOCAB, "teacher": "tied", "divergence": "forward",
                    "temperature": 1.0},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                         "cpu_model": _cpu_model(),
                          "sample": f"{CPU_ROWS} rows x {args.steps} steps, reference torch path (backend='torch')"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -414,7 +811,13 @@ def run_ours(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, sample, kind = _cpu_reference_rows(torch, CPU_ROWS, args.divergence)
-        cpu = {"value": v, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": kind, "sample": sample}
+        cpu = {"value": v, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": kind, "sample": sample,
+               "cpu_model": _cpu_model()}
+
+    extras = None
+    if not args.no_extras:
+        del phase_ev
+        extras = run_extras(args, torch, dev, pg, world, rank, reserve, (hs, ht, w, labels))
 
     if rank == 0:
         line = {
@@ -445,6 +848,7 @@ def run_ours(args):
             "e2e": e2e,
             "cpu_baseline": cpu,
             "loss": float(out.loss.detach()),
+            "extra_workloads": extras,
         }
         print(json.dumps(line))
     if pg is not None:

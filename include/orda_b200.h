@@ -21,8 +21,10 @@
  *   - Errors detected on the device (label out of range with validate_labels, a pipeline wait
  *     that timed out) are written to *device_status (int32, device memory, zero on entry); the
  *     caller reads it whenever it chooses. Kernels never trap.
- *   - Thread-safe and re-entrant: no global mutable state besides a per-process cache of the
- *     driver entry point used to encode TMA descriptors and an atomic launch counter.
+ *   - Thread-safe and re-entrant. Global state: a per-process cache of the driver entry points
+ *     used to encode TMA descriptors, an atomic launch counter, and one exception, the scratch
+ *     array of orda_distill_fwdbwd_static_ws (32 MiB of device memory per GPU, shared by every
+ *     call of that entry point; see its comment). No other entry point touches that array.
  */
 #ifndef ORDA_B200_H_
 #define ORDA_B200_H_
@@ -188,7 +190,9 @@ int32_t orda_distill_fwdbwd(const orda_distill_args_t* args, void* workspace, si
  * the library keeps until the process exits; the call allocates nothing. Rows are processed in
  * chunks small enough to fit; if even one 128-row chunk (or the per-row loss buffer, 3 x n_rows
  * floats) does not fit, it returns ORDA_ERR_WORKSPACE and launches nothing. The first call on each
- * device looks up the array's device address (make it before any stream capture). All calls share
+ * device looks up the array's device address (make it before any stream capture); the address is
+ * cached per device together with the CUDA context it was looked up in, and looked up again if the
+ * device's context changed (for example after cudaDeviceReset). All calls share
  * the one array: calls that overlap on the GPU (other streams, other host threads) race and must be
  * serialised by the caller. */
 int32_t orda_distill_fwdbwd_static_ws(const orda_distill_args_t* args, void* stream);

@@ -37,6 +37,12 @@ int32_t orda_debug_gemm_wide(int32_t dtype, int32_t a_mn, int32_t b_mn, const vo
  * 7 tiles. Synchronous; `reset` != 0 zeroes the counters afterwards. */
 int32_t orda_debug_gemm_profile(uint64_t* out, int32_t reset);
 
+/* Bounded-wait check: one thread waits on an mbarrier that nothing arrives at, with the same bounded
+ * wait the GEMM pipelines use but a limit of limit_ns (<= the library's 2 s bound). The wait gives
+ * up, writes ORDA_ERR_TIMEOUT to *status (device int32, zero on entry), stores the time it waited in
+ * *waited_ns (device uint64) and the kernel returns, leaving the context usable. */
+int32_t orda_debug_wait_timeout(int32_t* status, uint64_t limit_ns, uint64_t* waited_ns, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -867,16 +867,42 @@ static __device__ __align__(256) uint8_t g_orda_static_ws[ORDA_STATIC_WORKSPACE_
 namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_static_ws_mutex;
+// per device: the array's device address and the context it was looked up in
 void* g_static_ws_ptr[kMaxDevices] = {};
+void* g_static_ws_ctx[kMaxDevices] = {};
 
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
+// The current driver context (null if none or the entry point is unavailable).
+void* current_context() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  CUcontext ctx = nullptr;
+  if (fn && fn(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+  return ctx;
+}
+
+// Device address of the scratch array on the current device, looked up once per device (with that
+// device current) and again whenever the device's context differs from the one it was looked up in
+// (a reset context reloads the module, which moves the array).
 int static_ws_address(void** out) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return ORDA_ERR_NO_DEVICE;
   std::lock_guard<std::mutex> lock(g_static_ws_mutex);
-  if (!g_static_ws_ptr[dev]) {
+  // cudaGetSymbolAddress makes the primary context current if needed, so it runs before the
+  // context is read
+  if (!g_static_ws_ptr[dev] || g_static_ws_ctx[dev] != current_context()) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_orda_static_ws) != cudaSuccess || !p) return ORDA_ERR_CUDA;
     g_static_ws_ptr[dev] = p;
+    g_static_ws_ctx[dev] = current_context();
   }
   *out = g_static_ws_ptr[dev];
   return ORDA_OK;
@@ -903,6 +929,28 @@ extern "C" int32_t orda_distill_fwdbwd_static_ws(const orda_distill_args_t* args
   if (cudaMemsetAsync(static_cast<uint8_t*>(ws) + P.off_label, 0, P.off_row_stats - P.off_label, s) != cudaSuccess)
     return ORDA_ERR_CUDA;
   return dispatch_all(args, P, static_cast<uint8_t*>(ws), s);
+}
+
+// Testing hook: one thread waits on an mbarrier that nothing ever arrives at, with the library's
+// bounded wait and a caller-given limit. The wait must give up, flag ORDA_ERR_TIMEOUT in *status and
+// let the kernel return normally.
+namespace {
+__global__ void wait_timeout_kernel(int32_t* status, uint64_t limit_ns, uint64_t* waited_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  const uint32_t b = static_cast<uint32_t>(__cvta_generic_to_shared(&bar));
+  mbar_init(b, 1);
+  fence_barrier_init();
+  const uint64_t t0 = global_timer_ns();
+  const bool ok = mbar_wait(b, 0, status, limit_ns);  // phase 0 never completes
+  *waited_ns = ok ? 0ull : global_timer_ns() - t0;
+}
+}  // namespace
+
+extern "C" int32_t orda_debug_wait_timeout(int32_t* status, uint64_t limit_ns, uint64_t* waited_ns, void* stream) {
+  if (!status || !waited_ns || limit_ns == 0 || limit_ns > ORDA_WAIT_TIMEOUT_NS) return ORDA_ERR_INVALID_ARGUMENT;
+  count_launch();
+  wait_timeout_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(status, limit_ns, waited_ns);
+  return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
 }
 
 extern "C" int32_t orda_debug_gemm_profile(uint64_t* out, int32_t reset) {

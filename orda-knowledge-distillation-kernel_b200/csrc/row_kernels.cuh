@@ -46,7 +46,8 @@ struct RowParams {
 
 constexpr float kLog2e = 1.4426950408889634f;
 
-// 2^x with the hardware approximation (the same instruction __expf uses after scaling by log2 e).
+// 2^x with the PTX ex2.approx instruction. Callers evaluate exp(x) through the identity
+// exp(x) = 2^(x * log2 e), folding the log2 e factor into the arguments they already scale.
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

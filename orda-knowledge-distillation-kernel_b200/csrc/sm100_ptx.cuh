@@ -66,7 +66,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 
 // Bounded wait. Returns false (after flagging the status word) on timeout or when another role of
 // the same launch already flagged an error; callers then unwind without issuing further work.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int32_t* status) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int32_t* status,
+                                          uint64_t limit_ns = ORDA_WAIT_TIMEOUT_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   uint32_t spins = 0;
@@ -74,7 +75,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int32_t
     if (mbar_try_wait(bar, parity)) return true;
     if ((++spins & 63u) == 0) {
       if (*reinterpret_cast<volatile int32_t*>(status) != 0) return false;
-      if (global_timer_ns() - t0 > ORDA_WAIT_TIMEOUT_NS) {
+      if (global_timer_ns() - t0 > limit_ns) {
         atomicCAS(status, 0, ORDA_ERR_TIMEOUT);
         return false;
       }

@@ -97,6 +97,7 @@ EXPORTED_SYMBOLS = (
     "orda_debug_gemm_pair",
     "orda_debug_gemm_profile",
     "orda_debug_gemm_wide",
+    "orda_debug_wait_timeout",
 )
 
 _lib = None
@@ -140,6 +141,8 @@ def _declare(lib):
     lib.orda_debug_gemm_wide.argtypes = lib.orda_debug_gemm.argtypes
     lib.orda_debug_gemm_profile.restype = _i32
     lib.orda_debug_gemm_profile.argtypes = [ctypes.c_void_p, _i32]
+    lib.orda_debug_wait_timeout.restype = _i32
+    lib.orda_debug_wait_timeout.argtypes = [_vp, ctypes.c_uint64, _vp, _vp]
 
 
 def load(path: str | None = None):

@@ -114,6 +114,24 @@ class _NativeShardOps:
                                                    None if row_sums is None else row_sums.data_ptr(), self.stream),
                       "orda_shard_backward")
 
+    def release(self):
+        self.ws = None
+
+
+def _check_shard_status(pr, group) -> None:
+    """Raise on every rank if any rank's kernels reported a device error (a bounded pipeline wait
+    that timed out, or an out-of-range label under validation). The status words are combined with
+    a MAX all-reduce first, so no rank returns garbage gradients or is left waiting in a later
+    collective while another rank raises."""
+    status = getattr(pr, "status", None)
+    if status is None:
+        return
+    word = status.reshape(1).to(torch.int32).clone()
+    dist.all_reduce(word, op=dist.ReduceOp.MAX, group=group)
+    code = int(word.item())
+    if code != _native.OK:
+        raise RuntimeError(f"vocab-sharded distillation: device status on some rank: {_native.status_string(code)}")
+
 
 def _all_gather_records(local: torch.Tensor, world: int, group) -> torch.Tensor:
     """[world, n, ROW_STATS] gather of every rank's row records (one collective on NCCL; the list form
@@ -145,7 +163,15 @@ class _VocabShardFunction(torch.autograd.Function):
             row_sums = ops.jsd_partials(pr, row_stats)
             dist.all_reduce(row_sums, group=group)
         ops.backward(pr, row_stats, row_sums)
-        # the hidden-state gradients are sums over the vocab shards
+        # The workspace holds this shard's n_rows x V_local logits; nothing after the backward phase
+        # reads it, so it goes back to the allocator now rather than living as long as the graph.
+        release = getattr(ops, "release", None)
+        if release is not None:
+            release()
+        _check_shard_status(pr, group)
+        # The hidden-state gradients are sums over the vocab shards. Each rank's partial is in the
+        # compute dtype (one rounding per partial, like the single-GPU path's 16-bit output) and the
+        # collective sums those partials.
         for g in (pr.g_hs, pr.g_ht):
             if g is not None:
                 dist.all_reduce(g, group=group)
@@ -153,7 +179,7 @@ class _VocabShardFunction(torch.autograd.Function):
         loss = out[_native.OUT_LOSS].clone()
         ce_s, ce_t, kl = (out[i].clone() for i in (_native.OUT_STUDENT_CE, _native.OUT_TEACHER_CE, _native.OUT_KL))
         ctx.save_for_backward(pr.g_hs, pr.g_ht, pr.g_w, pr.g_wt, out[_native.OUT_MEAN_SCALE].clone())
-        ctx.ops = ops
+        ctx.rescale = ops.rescale  # only the (static) rescale is needed later, not the shard's buffers
         ctx.shapes = (student_hidden.shape[1], pr.h_t)
         ctx.dtypes = (student_hidden.dtype, teacher_hidden.dtype if teacher_hidden is not None else None,
                       weight.dtype, teacher_weight.dtype if teacher_weight is not None else None)
@@ -168,7 +194,7 @@ class _VocabShardFunction(torch.autograd.Function):
             return (None,) * 11
         h, h_t = ctx.shapes
         dt_hs, dt_ht, dt_w, dt_wt = ctx.dtypes
-        r = ctx.ops.rescale(ctx, [(g_hs, h, dt_hs), (g_ht, h_t, dt_ht), (g_w, h, dt_w), (g_wt, h_t, dt_wt)],
+        r = ctx.rescale(ctx, [(g_hs, h, dt_hs), (g_ht, h_t, dt_ht), (g_w, h, dt_w), (g_wt, h_t, dt_wt)],
                             grad_output)
         return (r[0], r[1], r[2], r[3], None, None, None, None, None, None, None)
 

@@ -85,6 +85,18 @@ def _rel_err(t, ref):
     return float(np.linalg.norm(a - ref) / max(np.linalg.norm(ref), 1e-30))
 
 
+def _row_rel_max(t, ref):
+    """Largest per-row relative error ||a_r - e_r|| / ||e_r|| (rows with a nonzero reference); rows
+    whose reference is exactly zero (ignored tokens) must be exactly zero. One bad row of dHidden, or
+    one bad vocabulary row of dW, shows here even where the tensor-wide norm dilutes it."""
+    a = t.detach().double().cpu().numpy()
+    en = np.linalg.norm(ref, axis=1)
+    dn = np.linalg.norm(a - ref, axis=1)
+    nz = en > 0
+    assert not np.any(np.linalg.norm(a[~nz], axis=1) > 0), "nonzero gradient on a row whose reference is zero"
+    return float(np.max(dn[nz] / en[nz])) if nz.any() else 0.0
+
+
 def _check_all(out, hs, weight, mode, teacher, tce, ref, *, atol_l, rtol_l, atol_g, rtol_g, check_kl=True):
     _close(out.loss, ref.loss, atol=atol_l, rtol=rtol_l, name="loss")
     _close(out.student_ce, ref.student_ce, atol=atol_l, rtol=rtol_l, name="student_ce")
@@ -264,9 +276,13 @@ def test_divergence_variants_bf16(mode, div, beta, temperature):
     _close(out.kl, ref.kl, atol=1e-5, rtol=1e-3, name="kl")
     assert _rel_err(hs.grad, ref.d_student_hidden) < 2e-2
     assert _rel_err(weight.grad, ref.d_weight) < 2e-2
+    assert _row_rel_max(hs.grad, ref.d_student_hidden) < 2e-2
+    assert _row_rel_max(weight.grad, ref.d_weight) < 2e-2
     if mode == "separate-full":
         assert _rel_err(teacher.hidden.grad, ref.d_teacher_hidden) < 2e-2
         assert _rel_err(teacher.weight.grad, ref.d_teacher_weight) < 2e-2
+        assert _row_rel_max(teacher.hidden.grad, ref.d_teacher_hidden) < 2e-2
+        assert _row_rel_max(teacher.weight.grad, ref.d_teacher_weight) < 2e-2
 
 
 # ----------------------------------------------------------------- benchmark config 1 (fp32, full size)
@@ -387,6 +403,8 @@ def test_config2_precomputed_slice():
     _close(out.loss, ref.loss, atol=0.0, rtol=1e-3, name="loss")
     assert _rel_err(hs.grad, ref.d_student_hidden) < 2e-2
     assert _rel_err(w.grad, ref.d_weight) < 2e-2
+    assert _row_rel_max(hs.grad, ref.d_student_hidden) < 2e-2
+    assert _row_rel_max(w.grad, ref.d_weight) < 2e-2
 
 
 @pytest.mark.parametrize("div", ["forward", "reverse", "jsd"])
@@ -409,6 +427,8 @@ def test_config3_llama_shape_slice(div):
     _close(out.kl, ref.kl, atol=0.0, rtol=1e-3, name="kl")
     assert _rel_err(hs.grad, ref.d_student_hidden) < 2e-2
     assert _rel_err(w.grad, ref.d_weight) < 2e-2
+    assert _row_rel_max(hs.grad, ref.d_student_hidden) < 2e-2
+    assert _row_rel_max(w.grad, ref.d_weight) < 2e-2
 
 
 def test_backward_scales_by_grad_output_and_supports_retain_graph():

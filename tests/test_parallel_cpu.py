@@ -4,6 +4,8 @@ returns the single-process loss (global mean over all ranks' rows) and the same 
 from __future__ import annotations
 
 import os
+import socket
+from datetime import timedelta
 
 import pytest
 import torch
@@ -12,6 +14,14 @@ import torch.multiprocessing as mp
 import torch.nn.functional as F
 
 from orda_ce_kernel import DistillationLossOutput, TiedTeacher
+
+
+def _free_port() -> int:
+    """A port no other listener holds right now (bound to 0, then released), so parallel test runs
+    do not collide at rendezvous."""
+    with socket.socket(socket.AF_INET, socket.SOCK_STREAM) as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
 
 
 def _formula(hs, w, labels, teacher, *, reduction="sum", kl_weight=0.0, kl_temperature=1.0, ignore_index=-100,
@@ -61,7 +71,7 @@ def test_token_parallel_matches_single_process():
     labels[[1, 4, 15, 16]] = -100
     with mp.Manager() as m:
         results = m.dict()
-        mp.spawn(_worker, args=(2, 29531, (hs, ht, w, labels), results), nprocs=2, join=True)
+        mp.spawn(_worker, args=(2, _free_port(), (hs, ht, w, labels), results), nprocs=2, join=True)
         results = dict(results)
     a, b, c = hs.clone().requires_grad_(True), ht.clone().requires_grad_(True), w.clone().requires_grad_(True)
     ref = _formula(a, c, labels, TiedTeacher(b), reduction="mean", kl_weight=0.3, kl_temperature=1.5)
@@ -102,6 +112,7 @@ class _TorchShardOps:
         pr.g_w = torch.zeros_like(pr.w) if w.requires_grad else None
         pr.g_wt = None
         pr.out = torch.zeros(_native.OUT_SLOTS, dtype=torch.float64)
+        pr.status = torch.zeros(1, dtype=torch.int32)
         return pr
 
     def _label_col(self, pr):
@@ -257,8 +268,7 @@ def test_vocab_parallel_matches_single_process(div):
     labels[::5] = -100
     with mp.Manager() as m:
         results = m.dict()
-        port = {"forward": 29655, "reverse": 29656, "jsd": 29657}[div]
-        mp.spawn(_vocab_worker, args=(2, port, (hs, ht, w, labels), div, results), nprocs=2, join=True)
+        mp.spawn(_vocab_worker, args=(2, _free_port(), (hs, ht, w, labels), div, results), nprocs=2, join=True)
         results = dict(results)
     ref = distill_reference(hs.numpy(), w.numpy(), labels.numpy(), mode="tied", teacher_hidden=ht.numpy(),
                             student_ce_weight=0.7, kl_weight=0.4, kl_temperature=1.5, kl_divergence=div,
@@ -270,3 +280,88 @@ def test_vocab_parallel_matches_single_process(div):
         np.testing.assert_allclose(ghs.numpy(), 2.0 * ref.d_student_hidden, rtol=1e-9, atol=1e-12)
         np.testing.assert_allclose(ght.numpy(), 2.0 * ref.d_teacher_hidden, rtol=1e-9, atol=1e-12)
         np.testing.assert_allclose(gw.numpy(), 2.0 * ref.d_weight[lo:hi], rtol=1e-9, atol=1e-12)
+
+
+# ------------------------------------------------------------------------------ failure handling
+class _FailingShardOps(_TorchShardOps):
+    """Shard ops whose backward on rank 1 reports a device error in the status word, the way a
+    bounded pipeline wait that ran out (ORDA_ERR_TIMEOUT) reports it from the kernels."""
+
+    def backward(self, pr, rs, row_sums):
+        from orda_ce_kernel import _native
+
+        super().backward(pr, rs, row_sums)
+        if dist.get_rank() == 1:
+            pr.status.fill_(_native.ERR_TIMEOUT)
+
+
+def _status_worker(rank, world, port, inputs, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=30))
+    from orda_ce_kernel.parallel import vocab_parallel_distillation_loss
+
+    hs0, ht0, w_all, labels = inputs
+    v = w_all.shape[0]
+    lo, hi = rank * v // world, (rank + 1) * v // world
+    try:
+        vocab_parallel_distillation_loss(hs0.clone().requires_grad_(True), w_all[lo:hi].clone().requires_grad_(True),
+                                         labels, TiedTeacher(ht0.clone()), vocab_offset=lo, vocab_total=v,
+                                         kl_weight=0.4, _shard_ops=_FailingShardOps)
+        results[rank] = "returned"
+    except RuntimeError as e:
+        results[rank] = str(e)
+    dist.destroy_process_group()
+
+
+def test_vocab_parallel_device_status_raises_on_every_rank():
+    """A device error reported by one rank's kernels makes every rank raise (the status words are
+    MAX-all-reduced before any gradient is returned), instead of one rank raising while the other
+    goes on with garbage gradients."""
+    g = torch.Generator().manual_seed(5)
+    n, h, v = 9, 4, 11
+    inputs = (torch.randn(n, h, generator=g, dtype=torch.float64), torch.randn(n, h, generator=g, dtype=torch.float64),
+              torch.randn(v, h, generator=g, dtype=torch.float64), torch.randint(0, v, (n,), generator=g))
+    with mp.Manager() as m:
+        results = m.dict()
+        mp.spawn(_status_worker, args=(2, _free_port(), inputs, results), nprocs=2, join=True)
+        results = dict(results)
+    for rank in (0, 1):
+        assert "timed out" in results[rank], results[rank]
+
+
+def _dead_rank_worker(rank, world, port, inputs, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=3))
+    from orda_ce_kernel.parallel import vocab_parallel_distillation_loss
+
+    hs0, ht0, w_all, labels = inputs
+    v = w_all.shape[0]
+    lo, hi = rank * v // world, (rank + 1) * v // world
+    if rank == 1:
+        # this rank fails on the host before its first collective and never joins it
+        results[rank] = "failed before the collective"
+        return
+    try:
+        vocab_parallel_distillation_loss(hs0.clone().requires_grad_(True), w_all[lo:hi].clone().requires_grad_(True),
+                                         labels, TiedTeacher(ht0.clone()), vocab_offset=lo, vocab_total=v,
+                                         kl_weight=0.4, _shard_ops=_TorchShardOps)
+        results[rank] = "returned"
+    except RuntimeError as e:
+        results[rank] = "error: " + str(e).splitlines()[0]
+
+
+def test_vocab_parallel_rank_failure_ends_the_collective_with_an_error():
+    """A rank that fails before the record gather leaves the surviving rank's collective to end with
+    an error (the process group's short timeout, or the closed connection), never to wait forever."""
+    g = torch.Generator().manual_seed(6)
+    n, h, v = 9, 4, 11
+    inputs = (torch.randn(n, h, generator=g, dtype=torch.float64), torch.randn(n, h, generator=g, dtype=torch.float64),
+              torch.randn(v, h, generator=g, dtype=torch.float64), torch.randint(0, v, (n,), generator=g))
+    with mp.Manager() as m:
+        results = m.dict()
+        mp.spawn(_dead_rank_worker, args=(2, _free_port(), inputs, results), nprocs=2, join=True)
+        results = dict(results)
+    assert results[1] == "failed before the collective"
+    assert results[0].startswith("error:"), results[0]
