@@ -62,6 +62,9 @@ def _args():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-extras", action="store_true", help="skip the extra_workloads measurements")
     p.add_argument("--only-extras", default="", help="comma-separated extra workload keys to run (default: all)")
+    p.add_argument("--dw-exchange", default="peer", choices=["peer", "nccl"],
+                   help="N>1: sum the lm_head gradient through peer memory (fused into the dW GEMM's epilogue) "
+                        "or with an NCCL all-reduce")
     p.add_argument("--reserve-sms", type=int, default=-1,
                    help="SMs the dHidden GEMM leaves to the overlapped dW all-reduce (N>1; -1: default)")
     return p.parse_args()
@@ -351,7 +354,7 @@ def _roof(flops_tok, tokens_per_gpu, ms):
             "peak_source": src}
 
 
-def run_extras(args, torch, dev, pg, world, rank, reserve, main_inputs):
+def run_extras(args, torch, dev, pg, world, rank, reserve, main_inputs, exchange=None):
     """The other benchmark configurations, measured in the same process after the headline run."""
     import orda_ce_kernel as ok
     from orda_ce_kernel import _fused
@@ -367,18 +370,18 @@ def run_extras(args, torch, dev, pg, world, rank, reserve, main_inputs):
         torch.cuda.synchronize()
         torch.cuda.empty_cache()
 
-    def dp_step(w, kw_fn, done):
+    def dp_step(w, kw_fn, done, ex=None):
         """One token-sharded step (distillation_loss + backward; with N > 1 the lm_head gradient is
-        all-reduced on a comm stream beside the dHidden GEMM, like the headline run)."""
+        summed over the ranks beside the dHidden GEMM, like the headline run)."""
         comm = torch.cuda.Stream(device=dev) if pg is not None else None
 
         def step(evs):
             w.grad = None
             with _fused.instrument(phase_events=evs, dweight_done_event=done, dweight_first=pg is not None,
-                                   reserve_sms=reserve):
+                                   reserve_sms=reserve, peer_exchange=ex):
                 out = kw_fn()
                 out.loss.backward()
-            if pg is not None:
+            if pg is not None and ex is None:
                 import torch.distributed as dist
 
                 comm.wait_event(done)
@@ -451,7 +454,12 @@ def run_extras(args, torch, dev, pg, world, rank, reserve, main_inputs):
             return ok.distillation_loss(hs5, w5, lab5, ok.TiedTeacher(ht5), kl_weight=1.0, kl_temperature=1.0,
                                         kl_divergence="jsd", jsd_beta=0.5)
 
-        ms, ph = _timed(torch, dp_step(w5, call5, done), max(2, steps // 2), warmup, pg, dev, True)
+        ex5 = None
+        if exchange is not None:
+            from orda_ce_kernel.parallel import PeerGradientExchange
+
+            ex5 = exchange if exchange.grad.shape == w5.shape else PeerGradientExchange(w5, group=pg)
+        ms, ph = _timed(torch, dp_step(w5, call5, done, ex5), max(2, steps // 2), warmup, pg, dev, True)
         results.append({"key": "config5", "workload": f"config 5: N=65536 (2x32768) split over {world} GPU(s) "
                         f"({rows} tokens each), tied teacher, JSD beta=0.5, T=1, H=4096, V=128256",
                         "value": N5 / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "scaling": "strong",
@@ -471,7 +479,7 @@ def run_extras(args, torch, dev, pg, world, rank, reserve, main_inputs):
                 return ok.distillation_loss(hs5, w5, lab5, ok.PrecomputedTeacher(logits=tl5), kl_weight=1.0,
                                             kl_temperature=1.0, kl_divergence="jsd", jsd_beta=0.5, config=cfg)
 
-            ms, ph = _timed(torch, dp_step(w5, call5p, done), max(2, steps // 2), warmup, pg, dev, True)
+            ms, ph = _timed(torch, dp_step(w5, call5p, done, ex5), max(2, steps // 2), warmup, pg, dev, True)
             line = _precomputed_line("config5_precomputed", f"config 5 precomputed variant: fp32 teacher log-probs "
                                      f"(N(0,2) before log_softmax), N=65536 split over {world} GPU(s), JSD beta=0.5, "
                                      f"T=1, H=4096, V=128256, {PRECOMP_CHUNK}-row chunks",
@@ -687,16 +695,22 @@ def run_ours(args):
 
     done = primed(torch.cuda.Event()) if pg is not None else None
 
-    reserve = (args.reserve_sms if args.reserve_sms >= 0 else default_reserve_sms(world)) if pg is not None else 0
+    exchange = None
+    if pg is not None and args.dw_exchange == "peer":
+        from orda_ce_kernel.parallel import PeerGradientExchange
+
+        exchange = PeerGradientExchange(w, group=pg)
+    reserve = (args.reserve_sms if args.reserve_sms >= 0 else default_reserve_sms(world)) \
+        if pg is not None and exchange is None else 0
 
     def step(h, t, lab, events=None):
         h.grad = None
         w.grad = None
         with _fused.instrument(phase_events=events, dweight_done_event=done, dweight_first=pg is not None,
-                               reserve_sms=reserve):
+                               reserve_sms=reserve, peer_exchange=exchange):
             out = ok.distillation_loss(h, w, lab, ok.TiedTeacher(t), **kw)
             out.loss.backward()
-        if pg is not None:
+        if pg is not None and exchange is None:
             import torch.distributed as dist
 
             # the lm_head gradient of the token shards is summed over the ranks (NCCL over NVLink),
@@ -817,7 +831,7 @@ def run_ours(args):
     extras = None
     if not args.no_extras:
         del phase_ev
-        extras = run_extras(args, torch, dev, pg, world, rank, reserve, (hs, ht, w, labels))
+        extras = run_extras(args, torch, dev, pg, world, rank, reserve, (hs, ht, w, labels), exchange)
 
     if rank == 0:
         line = {
@@ -829,6 +843,10 @@ def run_ours(args):
                             "V=128256, forward KL (T=1, weight 1), teacher CE 1.0, dHidden + dW",
                 "tokens_per_gpu": rows, "hidden": HID, "vocab": VOCAB, "divergence": args.divergence,
                 "parallelism": f"token-sharded dp{world}" if world > 1 else "single GPU",
+                "lm_head_grad_exchange": (("peer memory: rows routed to their owners from the dW GEMM epilogue, "
+                                           "owners sum and broadcast beside the dHidden GEMM")
+                                          if exchange is not None else "NCCL all-reduce on a side stream")
+                if world > 1 else None,
                 "overlap_reserve_sms": reserve,
                 "l2": "inputs larger than L2 (lm_head 1.05 GB, logits workspace 4.2 GB)",
             },

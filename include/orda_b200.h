@@ -197,6 +197,64 @@ int32_t orda_distill_fwdbwd(const orda_distill_args_t* args, void* workspace, si
  * serialised by the caller. */
 int32_t orda_distill_fwdbwd_static_ws(const orda_distill_args_t* args, void* stream);
 
+/* ---- token-sharded multi-GPU: lm_head gradient exchanged over peer memory ----
+ * The reference has no multi-GPU code; this replaces the all-reduce of the lm_head gradient that
+ * data parallelism needs after TiedCEFunction / SeparateFullCEFunction (ops/tied_teacher.py:481-495,
+ * ops/separate_teacher.py:926-934 compute it per process). Every rank owns one slab of lm_head rows:
+ * rows [r * slab_rows, (r + 1) * slab_rows) belong to rank r. Each rank exposes two buffers mapped
+ * into every peer's address space (CUDA IPC / symmetric memory, set up by the caller):
+ *   slots: [world * slab_rows, hidden] in the compute dtype - slot k receives rank k's partial
+ *          gradient of this rank's slab;
+ *   grad:  [vocab, hidden] in the compute dtype - the summed lm_head gradient, written by every owner.
+ * No kernel of this library waits on another GPU: the caller orders the phases with its own
+ * collective (e.g. a one-element NCCL all-reduce) between them. */
+#define ORDA_MAX_PEERS 8
+
+typedef struct orda_peer_slots {
+  int32_t world;                        /* ranks (1..ORDA_MAX_PEERS)                                 */
+  int32_t rank;                         /* this rank                                                 */
+  int64_t slab_rows;                    /* lm_head rows owned per rank (ceil(vocab / world) or more)  */
+  void* slot_base[ORDA_MAX_PEERS];      /* device address of rank k's slots buffer, as mapped here   */
+  void* grad_base[ORDA_MAX_PEERS];      /* device address of rank k's grad buffer, as mapped here    */
+} orda_peer_slots_t;
+
+/* Mapping a buffer of one process into another process on the same node (plain CUDA IPC peer
+ * mappings, no multicast objects), for the slots / grad buffers above. `ptr` may point anywhere
+ * inside a device allocation (e.g. one made by a caching allocator); the handle carries the offset. */
+typedef struct orda_ipc_handle {
+  uint8_t handle[64];  /* cudaIpcMemHandle_t of the allocation that contains ptr */
+  uint64_t offset;     /* ptr - allocation base                                  */
+} orda_ipc_handle_t;
+
+/* Describes `ptr` (device memory of the current device) for orda_ipc_import in another process. */
+int32_t orda_ipc_export(const void* ptr, orda_ipc_handle_t* out);
+
+/* Maps the exporter's allocation into this process (peer access over NVLink) and returns the
+ * address of the exported pointer. Close it with orda_ipc_close when done. */
+int32_t orda_ipc_import(const orda_ipc_handle_t* handle, void** ptr_out);
+
+/* Unmaps an address returned by orda_ipc_import (with the handle it came from). */
+int32_t orda_ipc_close(void* ptr, const orda_ipc_handle_t* handle);
+
+/* orda_distill_fwdbwd with the student lm_head gradient routed to its owners: the dW GEMM of the
+ * last row chunk stores row v of this rank's partial gradient into slot `rank` of the owner of v
+ * (peer stores from the GEMM epilogue, overlapped with the GEMM's remaining tiles). Earlier chunks
+ * accumulate in args->grad_weight, which the last chunk adds in; grad_weight may be this rank's own
+ * grad buffer. 16-bit compute dtype, grad_weight_fp32 = 0, vocab_offset = 0. The routed stores are
+ * complete and visible system-wide when the kernel that made them has finished (dweight_done_event
+ * marks that point on `stream`). */
+int32_t orda_distill_fwdbwd_peer(const orda_distill_args_t* args, void* workspace, size_t workspace_bytes,
+                                 const orda_peer_slots_t* peers, void* stream);
+
+/* Phase 2, after every rank's routed dW GEMM has finished (the caller's barrier): this rank sums
+ * the `world` slots of its slab (fp32 accumulation, one rounding) and writes the sum into the grad
+ * buffer of every rank (peer stores), so each grad buffer ends up holding the summed [vocab, hidden]
+ * gradient once all ranks have run this (the caller's second barrier). dtype: ORDA_BF16 / ORDA_F16.
+ * `ctas` bounds the grid (0 = library default) so the kernel can run beside a GEMM on another
+ * stream. */
+int32_t orda_peer_reduce_broadcast(const orda_peer_slots_t* peers, int64_t vocab, int64_t hidden, int32_t dtype,
+                                   int32_t ctas, void* stream);
+
 /* ---- vocab-sharded multi-GPU building blocks (one call per rank; NCCL stays with the caller) ----
  * Per-row statistics record exchanged between ranks: ORDA_ROW_STATS floats per row. */
 #define ORDA_ROW_STATS 16

@@ -10,6 +10,22 @@
 namespace orda {
 
 constexpr int kTileRows = 128;   // rows of one GEMM tile (TMEM lanes)
+
+// The chunk workspace holds every logit as a base-2 exponent relative to its 128-column tile
+// maximum, y = (z - m_tile) * log2(e), in the compute dtype. exp(z - m) is then 2^y: one ex2 per
+// element with no scaling multiply, and the bf16 rounding of y has the same relative precision as
+// rounding z - m would have.
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// 2^x with the PTX ex2.approx instruction. Callers evaluate exp(x) through the identity
+// exp(x) = 2^(x * log2 e), folding the log2 e factor into the arguments they already scale.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 constexpr int kVocabTile = 128;  // vocab columns covered by one statistics record
 constexpr int kTileStats = 2;    // floats per (row, vocab tile) record
 constexpr int kRowStats = 16;    // floats per merged row record (== ORDA_ROW_STATS)
@@ -63,6 +79,19 @@ template <> struct Conv<__half> {
 };
 
 // Two floats rounded to the 16-bit type in one conversion, low half = a (memory order a, b).
+// The two 16-bit values of a packed word as floats (low half first, as pack2 stores them).
+template <typename T> __device__ __forceinline__ void unpack2(uint32_t w, float& a, float& b);
+template <> __device__ __forceinline__ void unpack2<__nv_bfloat16>(uint32_t w, float& a, float& b) {
+  a = __uint_as_float(w << 16);
+  b = __uint_as_float(w & 0xffff0000u);
+}
+template <> __device__ __forceinline__ void unpack2<__half>(uint32_t w, float& a, float& b) {
+  const __half2 h = *reinterpret_cast<const __half2*>(&w);
+  const float2 f = __half22float2(h);
+  a = f.x;
+  b = f.y;
+}
+
 template <typename T> __device__ __forceinline__ uint32_t pack2(float a, float b);
 template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);

@@ -5,8 +5,8 @@
 // un-shifted logits to memory:
 //   - the tile maxima (student and teacher),
 //   - the label logit (exact fp32 accumulator value),
-// and stores the logits shifted by the tile maximum into the bounded chunk workspace in the
-// compute dtype (values near the row maximum, which dominate softmax, keep full relative precision).
+// and stores the logits shifted by the tile maximum, as base-2 exponents, into the bounded chunk
+// workspace in the compute dtype (values near the row maximum, which dominate softmax, keep full relative precision).
 //
 // Together with row_stats_kernel this is the statistics half of the reference row kernels
 // (ops/tied_teacher.py:54-141, ops/separate_teacher.py, ops/precomputed_teacher.py:53-101).
@@ -35,6 +35,10 @@ struct FwdEpiParams {
   int32_t tg_dtype;
   float* tile_stats;              // [rows][n_vtiles][kTileStats]
   float* label_logits;            // [rows][2]
+  // Optional ([rows][n_vtiles] float2 {student, teacher}): per (row, vocab tile) sum of 2^y over the
+  // tile's stored base-2 exponents y, i.e. sum exp(z - m_tile). The wide GEMM's epilogue forms it
+  // after releasing the accumulator, from the tile it has just stored.
+  float* tile_sums;
   int32_t plain_teacher;          // wide kernel, A_PLAIN: the accumulators hold teacher logits
 };
 
@@ -112,7 +116,7 @@ __device__ __forceinline__ void fwd_tile_stats(const FwdEpiParams& p, int64_t ro
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       if (c * 32 + j == label_col) zy_s = v[j];
-      v[j] -= ms;
+      v[j] = (v[j] - ms) * kLog2e;
     }
     if (row_ok && (f & F_WRITE_WS_S)) store_chunk32<WsT>(static_cast<WsT*>(p.ws_s) + ws_row + c * 32, v);
     if (teacher) {
@@ -120,7 +124,7 @@ __device__ __forceinline__ void fwd_tile_stats(const FwdEpiParams& p, int64_t ro
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         if (c * 32 + j == label_col) zy_t = v[j];
-        v[j] -= mt;
+        v[j] = (v[j] - mt) * kLog2e;
       }
       if (row_ok && (f & F_WRITE_WS_T)) store_chunk32<WsT>(static_cast<WsT*>(p.ws_t) + ws_row + c * 32, v);
     }

@@ -33,6 +33,16 @@ struct StoreEpiParams {
   int64_t M, N;      // valid extent of D
   int32_t out_f32;   // 1: fp32 output, 0: compute dtype
   int32_t accumulate;// 1: D = out + acc
+  // Row routing to the owning GPU (fused reduce-scatter of a data-parallel weight gradient, 16-bit
+  // output only): with peers > 0, row v of D is stored to
+  //   peer_base[v / slab_rows] + (slot * slab_rows + v % slab_rows) * ldo
+  // (peer addresses mapped into this GPU's address space), and `accumulate` adds the local partial
+  // at acc_src + v * ldo instead of the destination's previous value.
+  int32_t peers;
+  int32_t slot;
+  int64_t slab_rows;
+  const void* acc_src;
+  void* peer_base[ORDA_MAX_PEERS];
 };
 
 struct TcGemmParams {
@@ -137,10 +147,20 @@ __device__ __forceinline__ void store_epilogue(const StoreEpiParams& st, uint32_
         for (int j = 0; j < cnt; ++j) o[j] = st.accumulate ? o[j] + v[j] : v[j];
       }
     } else {
-      T16* o = static_cast<T16*>(st.out) + row * st.ldo + col0;
+      T16* o;
+      const T16* prev_src;
+      if (st.peers > 0) {
+        const int64_t owner = row / st.slab_rows;
+        o = static_cast<T16*>(st.peer_base[owner]) + (st.slot * st.slab_rows + row - owner * st.slab_rows) * st.ldo +
+            col0;
+        prev_src = st.acc_src ? static_cast<const T16*>(st.acc_src) + row * st.ldo + col0 : nullptr;
+      } else {
+        o = static_cast<T16*>(st.out) + row * st.ldo + col0;
+        prev_src = o;
+      }
       if (cnt == 32 && (st.ldo % 8) == 0) {
-        if (st.accumulate) {
-          const uint4* i4 = reinterpret_cast<const uint4*>(o);
+        if (st.accumulate && prev_src) {
+          const uint4* i4 = reinterpret_cast<const uint4*>(prev_src);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const uint4 b = i4[q];
@@ -152,7 +172,7 @@ __device__ __forceinline__ void store_epilogue(const StoreEpiParams& st, uint32_
         store_chunk32<T16>(o, v);
       } else {
         for (int j = 0; j < cnt; ++j) {
-          const float prev = st.accumulate ? Conv<T16>::to_f(o[j]) : 0.f;
+          const float prev = st.accumulate && prev_src ? Conv<T16>::to_f(prev_src[j]) : 0.f;
           o[j] = Conv<T16>::from_f(prev + v[j]);
         }
       }

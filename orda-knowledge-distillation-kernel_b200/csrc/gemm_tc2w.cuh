@@ -49,7 +49,7 @@ struct WideShape {
 
 // Logits epilogue of one 256-column accumulator for the warp's 32 rows (one row per lane): per
 // 128-column vocab tile the tile maximum, the exact label logit and the logits shifted by the maximum
-// (16-bit, staged in the warp's 4 KB shared-memory buffer 64 columns at a time and written with TMA
+// as base-2 exponents (16-bit, staged in the warp's 4 KB shared-memory buffer 64 columns at a time and written with TMA
 // stores).
 template <typename WsT>
 __device__ __forceinline__ void wide_fwd_acc(const FwdEpiParams& p, const CUtensorMap* ws_map, bool write_ws,
@@ -102,6 +102,7 @@ __device__ __forceinline__ void wide_fwd_acc(const FwdEpiParams& p, const CUtens
       }
     }
     if (write_ws) {
+      const float mL = m * kLog2e;
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         // the previous TMA store of this warp must have read the staging buffer
@@ -111,10 +112,12 @@ __device__ __forceinline__ void wide_fwd_acc(const FwdEpiParams& p, const CUtens
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           const int c = hf * 2 + (q >> 2), e0 = (q & 3) * 8;
-          const uint32_t w0 = pack2<WsT>(__uint_as_float(r[c][e0]) - m, __uint_as_float(r[c][e0 + 1]) - m);
-          const uint32_t w1 = pack2<WsT>(__uint_as_float(r[c][e0 + 2]) - m, __uint_as_float(r[c][e0 + 3]) - m);
-          const uint32_t w2 = pack2<WsT>(__uint_as_float(r[c][e0 + 4]) - m, __uint_as_float(r[c][e0 + 5]) - m);
-          const uint32_t w3 = pack2<WsT>(__uint_as_float(r[c][e0 + 6]) - m, __uint_as_float(r[c][e0 + 7]) - m);
+          // base-2 exponents relative to the tile maximum: (z - m) * log2 e
+          auto y = [&](int e) { return fmaf(__uint_as_float(r[c][e]), kLog2e, -mL); };
+          const uint32_t w0 = pack2<WsT>(y(e0), y(e0 + 1));
+          const uint32_t w1 = pack2<WsT>(y(e0 + 2), y(e0 + 3));
+          const uint32_t w2 = pack2<WsT>(y(e0 + 4), y(e0 + 5));
+          const uint32_t w3 = pack2<WsT>(y(e0 + 6), y(e0 + 7));
           const uint32_t addr = staging + static_cast<uint32_t>(lane) * 128u +
                                 ((static_cast<uint32_t>(q) ^ static_cast<uint32_t>(lane & 7)) << 4);
           asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w0), "r"(w1), "r"(w2), "r"(w3)
@@ -132,6 +135,43 @@ __device__ __forceinline__ void wide_fwd_acc(const FwdEpiParams& p, const CUtens
       p.tile_stats[(row * p.n_vtiles + tile) * kTileStats + (student ? TS_MAX_S : TS_MAX_T)] = m;
       if (label_col >= 0) p.label_logits[row * 2 + (student ? 0 : 1)] = zy;
     }
+  }
+}
+
+// Softmax sums of the vocab tiles [n0, n0 + 256) of one row, read back from the workspace after this
+// warp's TMA stores of them have completed: per 128-column tile, sum 2^y over its valid columns (the
+// stored base-2 exponents relative to the tile maximum). Runs after the accumulator has been released,
+// so its ex2 work overlaps the next tile's MMAs instead of delaying them. Every lane reads its own
+// row (16-byte vectors through L2, where the stores have just landed).
+template <typename WsT>
+__device__ __forceinline__ void wide_tile_sums(const FwdEpiParams& p, int64_t row, int64_t n0, bool student) {
+  if (row >= p.rows) return;
+  const WsT* src = static_cast<const WsT*>(student ? p.ws_s : p.ws_t) + row * p.ld_ws + n0;
+  const int tile0 = static_cast<int>(n0 / kVocabTile);
+  const int ntiles = p.n_vtiles - tile0 < 2 ? p.n_vtiles - tile0 : 2;
+  for (int h = 0; h < ntiles; ++h) {
+    const int64_t nh = n0 + h * kVocabTile;
+    const int nvalid = static_cast<int>(p.vocab - nh < kVocabTile ? p.vocab - nh : kVocabTile);
+    uint4 v[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) v[k] = __ldcg(reinterpret_cast<const uint4*>(src + h * kVocabTile) + k);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const uint32_t w[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float a, b;
+        unpack2<WsT>(w[q], a, b);
+        const int col = k * 8 + q * 2;
+        if (nvalid == kVocabTile) {
+          acc[q] += ex2_approx(a) + ex2_approx(b);
+        } else {
+          acc[q] += (col < nvalid ? ex2_approx(a) : 0.f) + (col + 1 < nvalid ? ex2_approx(b) : 0.f);
+        }
+      }
+    }
+    p.tile_sums[(row * p.n_vtiles + tile0 + h) * 2 + (student ? 0 : 1)] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
   }
 }
 
@@ -393,11 +433,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WideShape<EPI>::kThr
           if (rank == 0) mbar_arrive(tempty_bar(j));
           else mbar_arrive_cluster(map_to_cta(tempty_bar(j), 0));
         }
+        if constexpr (EPI == EPI_FWD_STATS) {
+          if (p.fwd.tile_sums) {
+            // the accumulator is free again; the softmax sums come from the tile just stored
+            if (lane == 0) {
+              bulk_wait_all();
+              fence_proxy_async_global();
+            }
+            __syncwarp();
+            int64_t row, y0;
+            bool student;
+            if constexpr (AMODE == A_INTERLEAVE) {
+              student = quarter < 2;
+              y0 = static_cast<int64_t>(mt) * 256 + j * 128 + rank * 64 + (quarter & 1) * 32;
+            } else {
+              student = p.fwd.plain_teacher == 0;
+              y0 = static_cast<int64_t>(mt) * 512 + j * 256 + rank * 128 + quarter * 32;
+            }
+            row = y0 + lane;
+            wide_tile_sums<T16>(p.fwd, row, n0, student);
+          }
+        }
       }
       if (prof) busy += clk() - c1;
     }
     if constexpr (EPI == EPI_FWD_STATS) {
       if (lane == 0) bulk_wait_all();  // staged stores complete before the shared memory goes away
+    } else {
+      // stores routed to other GPUs are visible system-wide once this kernel has finished
+      if (p.st.peers > 0) __threadfence_system();
     }
     if (prof) {
       atomicAdd(&g_tc2_prof[p.prof_slot][3], static_cast<unsigned long long>(w_tfull));

@@ -104,7 +104,25 @@ struct Plan {
   int64_t part_cols;
   size_t off_part_records;
   size_t off_dh_split;  // fp32 partials of the k-split dHidden GEMM: [2][C][max(H, Ht)]
+  // Epilogue-statistics path: the logits epilogue sums each stored tile, so the row records come
+  // from the tile records (no statistics pass over the logits); the divergence row sums come from
+  // the dlogits sweep (forward KL) or one base-2 divergence sweep before it (reverse KL, JSD).
+  // 16-bit compute, T = 1, teacher logits from an accumulator (or no teacher), gradients
+  // requested, one GPU.
+  bool es;
+  size_t off_tile_sums;    // [C][n_vtiles] float2
+  size_t off_cross_parts;  // [parts][C] fp32
 };
+
+// ORDA_EPILOGUE_STATS=0 turns the epilogue-statistics path off (A/B measurements and tests of the
+// statistics-pass path on the same inputs).
+bool epilogue_stats_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("ORDA_EPILOGUE_STATS");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
 
 int check_args(const orda_distill_args_t* a) {
   if (!a || a->abi_version != ORDA_ABI_VERSION) return ORDA_ERR_INVALID_ARGUMENT;
@@ -124,7 +142,7 @@ int check_args(const orda_distill_args_t* a) {
   return ORDA_OK;
 }
 
-Plan make_plan(const orda_distill_args_t* a, int64_t chunk_override) {
+Plan make_plan(const orda_distill_args_t* a, int64_t chunk_override, bool allow_es = true) {
   Plan p{};
   const int mode = a->teacher_mode;
   p.teacher_ce = a->teacher_ce_weight != 0.f;
@@ -159,6 +177,8 @@ Plan make_plan(const orda_distill_args_t* a, int64_t chunk_override) {
   if (p.grad_t) f |= F_GRAD_T;
   if (a->validate_labels) f |= F_VALIDATE;
   p.flags = f;
+  p.es = allow_es && epilogue_stats_enabled() && a->compute_dtype != ORDA_F32 && !p.teacher_gmem &&
+         !p.t_not_one && p.any_grad;
 
   p.n_vtiles = cdiv(a->vocab, kVocabTile);
   p.vpad = p.n_vtiles * kVocabTile;
@@ -183,6 +203,10 @@ Plan make_plan(const orda_distill_args_t* a, int64_t chunk_override) {
   p.part_cols = cdiv(cdiv(a->vocab, p.parts), 256) * 256;
   p.off_part_records = off;
   if (p.parts > 1) off = align256(off + sizeof(float) * kRowStats * p.parts * p.C);
+  p.off_tile_sums = off;
+  if (p.es) off = align256(off + sizeof(float) * 2 * p.C * p.n_vtiles);
+  p.off_cross_parts = off;
+  if (p.es) off = align256(off + sizeof(float) * (p.jsd ? 2 : 1) * p.parts * p.C);
   p.off_dh_split = off;
   if (a->compute_dtype != ORDA_F32 && (a->need_grad_student_hidden || a->need_grad_teacher_hidden))
     off = align256(off + sizeof(float) * 2 * p.C * std::max(a->hidden, a->teacher_hidden));
@@ -226,6 +250,23 @@ bool gemm_profiling() {
   }();
   return on;
 }
+
+// Tile-raster grouping of the pair GEMMs (tile_coords: > 0 groups that many m tiles with m running
+// fastest, < 0 groups n tiles). Testing knob: ORDA_GROUP_LOGITS / ORDA_GROUP_DH / ORDA_GROUP_DW
+// replace the defaults, so the raster can be swept without a rebuild.
+int group_for(int role, int dflt) {
+  static int v[3] = {0, 0, 0};
+  static std::once_flag once;
+  std::call_once(once, [] {
+    const char* names[3] = {"ORDA_GROUP_LOGITS", "ORDA_GROUP_DH", "ORDA_GROUP_DW"};
+    for (int i = 0; i < 3; ++i) {
+      const char* e = getenv(names[i]);
+      v[i] = e ? atoi(e) : 0;
+    }
+  });
+  return v[role] != 0 ? v[role] : dflt;
+}
+enum GemmRole { ROLE_LOGITS = 0, ROLE_DH = 1, ROLE_DW = 2 };
 
 template <bool A_MN, bool B_MN, int AMODE, bool TWO_SEG, int EPI, typename T16>
 int launch_tc2(TcGemmParams& prm, int64_t M_tiles, int64_t N, cudaStream_t stream, int group_m,
@@ -297,11 +338,15 @@ RowParams row_params(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, c
   r.ld_row_losses = a->n_rows;
   r.ws_s = ws + P.off_ws_s; r.ws_t = ws + P.off_ws_t; r.ld_ws = P.vpad;
   r.t_gmem = c.tg; r.ld_tg = a->ld_teacher_logits; r.tg_dtype = a->teacher_logits_dtype;
+  r.tg_vec = c.tg && (reinterpret_cast<uintptr_t>(a->teacher_logits) & 15u) == 0 &&
+             (a->ld_teacher_logits * static_cast<int64_t>(esize(a->teacher_logits_dtype))) % 16 == 0;
   r.status = a->device_status;
   r.grad_scale = a->grads_include_mean_scale ? a->out_reduced + ORDA_OUT_MEAN_SCALE : nullptr;
   r.parts = P.parts;
   r.part_cols = P.part_cols;
   r.part_records = reinterpret_cast<float*>(ws + P.off_part_records);
+  r.tile_sums = P.es ? reinterpret_cast<const float*>(ws + P.off_tile_sums) : nullptr;
+  r.cross_parts = P.es && P.kl ? reinterpret_cast<float*>(ws + P.off_cross_parts) : nullptr;
   return r;
 }
 
@@ -318,6 +363,7 @@ FwdEpiParams fwd_params(const orda_distill_args_t* a, const Plan& P, uint8_t* ws
   f.t_gmem = c.tg; f.ld_tg = a->ld_teacher_logits; f.tg_dtype = a->teacher_logits_dtype;
   f.tile_stats = reinterpret_cast<float*>(ws + P.off_tile_stats);
   f.label_logits = reinterpret_cast<float*>(ws + P.off_label);
+  f.tile_sums = P.es ? reinterpret_cast<float*>(ws + P.off_tile_sums) : nullptr;
   return f;
 }
 
@@ -349,10 +395,12 @@ int forward_tc(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const C
     if ((rc = make_operand_map(&prm.a0, dt, c.hs, false, c.rows, a->hidden, a->ld_student_hidden, 64))) return rc;
     if ((rc = make_operand_map(&prm.a1, dt, c.ht, false, c.rows, a->hidden, a->ld_teacher_hidden, 64))) return rc;
     if ((rc = ws_store_maps(a, P, ws, c, prm))) return rc;
-    return launch_tc2w<false, false, A_INTERLEAVE, false, EPI_FWD_STATS, T16>(prm, cdiv(c.rows, 256), a->vocab, s, 8);
+    return launch_tc2w<false, false, A_INTERLEAVE, false, EPI_FWD_STATS, T16>(prm, cdiv(c.rows, 256), a->vocab, s,
+                                                                            group_for(ROLE_LOGITS, 8));
   }
   if ((rc = ws_store_maps(a, P, ws, c, prm))) return rc;
-  if ((rc = launch_tc2w<false, false, A_PLAIN, false, EPI_FWD_STATS, T16>(prm, cdiv(c.rows, 512), a->vocab, s, 4)))
+  if ((rc = launch_tc2w<false, false, A_PLAIN, false, EPI_FWD_STATS, T16>(prm, cdiv(c.rows, 512), a->vocab, s,
+                                                                        group_for(ROLE_LOGITS, 4))))
     return rc;
   if (P.teacher_acc) {
     // separate teacher (or precomputed teacher hidden + weight): a second wide launch over (ht, Wt)
@@ -362,7 +410,8 @@ int forward_tc(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const C
     if ((rc = make_operand_map(&pt.b0, dt, a->teacher_weight, false, a->vocab, a->teacher_hidden, a->ld_teacher_weight, kVocabTile))) return rc;
     pt.kb0 = static_cast<int32_t>(cdiv(a->teacher_hidden, kBK));
     pt.fwd.plain_teacher = 1;
-    return launch_tc2w<false, false, A_PLAIN, false, EPI_FWD_STATS, T16>(pt, cdiv(c.rows, 512), a->vocab, s, 4);
+    return launch_tc2w<false, false, A_PLAIN, false, EPI_FWD_STATS, T16>(pt, cdiv(c.rows, 512), a->vocab, s,
+                                                                         group_for(ROLE_LOGITS, 4));
   }
   return ORDA_OK;
 }
@@ -383,14 +432,16 @@ int dh_tc(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const void* 
   prm.kb0 = static_cast<int32_t>(cdiv(a->vocab, kBK));
   if (prm.kb0 < 2 || n % 8 != 0) {
     prm.st = StoreEpiParams{out, n, rows, n, 0, 0};
-    return launch_tc2<false, true, A_PLAIN, false, EPI_STORE, T16>(prm, cdiv(rows, 256), n, s, 8, reserve);
+    return launch_tc2<false, true, A_PLAIN, false, EPI_STORE, T16>(prm, cdiv(rows, 256), n, s, group_for(ROLE_DH, 8),
+                                                                    reserve);
   }
   float* part = reinterpret_cast<float*>(ws + P.off_dh_split);
   prm.ksplit = 2;
   prm.kb_split = static_cast<int32_t>(cdiv(prm.kb0, 2));
   prm.split_bytes = static_cast<int64_t>(sizeof(float)) * rows * n;
   prm.st = StoreEpiParams{part, n, rows, n, 1, 0};
-  if ((rc = launch_tc2w<false, true, A_PLAIN, false, EPI_STORE, T16>(prm, cdiv(rows, 512), n, s, 4, reserve)))
+  if ((rc = launch_tc2w<false, true, A_PLAIN, false, EPI_STORE, T16>(prm, cdiv(rows, 512), n, s, group_for(ROLE_DH, 4),
+                                                                     reserve)))
     return rc;
   const int64_t count8 = rows * n / 8;
   count_launch();
@@ -400,10 +451,12 @@ int dh_tc(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const void* 
 }
 
 // dW[V, N] (+)= dZ0^T H0 (+ dZ1^T H1)
+// With `route`, the rows of the result go to their owners' slots on the peer GPUs (accumulating the
+// local partial in `out` when `accumulate`) instead of into `out`.
 template <typename T16>
 int dw_tc(const orda_distill_args_t* a, const Plan& P, const void* dz0, const void* h0, int64_t ldh0, const void* dz1,
           const void* h1, int64_t ldh1, int64_t n, void* out, int out_f32, int accumulate, int64_t rows,
-          int32_t* status, cudaStream_t s) {
+          int32_t* status, cudaStream_t s, const orda_peer_slots_t* route = nullptr) {
   TcGemmParams prm{};
   prm.status = status;
   const int dt = a->compute_dtype;
@@ -412,13 +465,20 @@ int dw_tc(const orda_distill_args_t* a, const Plan& P, const void* dz0, const vo
   if ((rc = make_operand_map(&prm.b0, dt, h0, true, n, rows, ldh0, 128))) return rc;
   prm.kb0 = static_cast<int32_t>(cdiv(rows, kBK));
   prm.st = StoreEpiParams{out, n, a->vocab, n, out_f32, accumulate};
+  if (route) {
+    prm.st.peers = route->world;
+    prm.st.slot = route->rank;
+    prm.st.slab_rows = route->slab_rows;
+    prm.st.acc_src = accumulate ? out : nullptr;
+    for (int k = 0; k < route->world; ++k) prm.st.peer_base[k] = route->slot_base[k];
+  }
   if (dz1) {
     if ((rc = make_operand_map(&prm.a1, dt, dz1, true, a->vocab, rows, P.vpad, kTileRows))) return rc;
     if ((rc = make_operand_map(&prm.b1, dt, h1, true, n, rows, ldh1, 128))) return rc;
     prm.kb1 = prm.kb0;
-    return launch_tc2w<true, true, A_PLAIN, true, EPI_STORE, T16>(prm, cdiv(a->vocab, 512), n, s, 4);
+    return launch_tc2w<true, true, A_PLAIN, true, EPI_STORE, T16>(prm, cdiv(a->vocab, 512), n, s, group_for(ROLE_DW, 4));
   }
-  return launch_tc2w<true, true, A_PLAIN, false, EPI_STORE, T16>(prm, cdiv(a->vocab, 512), n, s, 4);
+  return launch_tc2w<true, true, A_PLAIN, false, EPI_STORE, T16>(prm, cdiv(a->vocab, 512), n, s, group_for(ROLE_DW, 4));
 }
 
 // ------------------------------------------------------------------ fp32 (SIMT) phases
@@ -460,6 +520,21 @@ int row_phases(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const C
   // one warp per (row, column part), 8 per block; the JSD sweep runs one warp per row
   const int sweep_grid = static_cast<int>(std::min<int64_t>(cdiv(c.rows * P.parts, 8), 16 * num_sms()));
   const int row_grid = static_cast<int>(std::min<int64_t>(cdiv(c.rows, 8), 16 * num_sms()));
+  if (P.es) {
+    // row records from the epilogue's tile records -> dlogits sweep (+ cross term) -> row losses
+    count_launch(3);
+    tile_merge_kernel<<<row_grid, 256, 0, s>>>(r);
+    if constexpr (sizeof(WsT) == 2) {
+      if (P.rev || P.jsd) {
+        count_launch();
+        if (P.jsd) div_sweep_kernel<WsT, DK_JSD><<<sweep_grid, 256, 0, s>>>(r);
+        else div_sweep_kernel<WsT, DK_REV><<<sweep_grid, 256, 0, s>>>(r);
+      }
+    }
+    launch_grad_sweep<WsT>(r, sweep_grid, s);
+    row_loss_kernel<<<static_cast<int>(cdiv(c.rows, 256)), 256, 0, s>>>(r);
+    return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
+  }
   if (do_merge) {
     count_launch();
     launch_row_stats<WsT>(r, sweep_grid, s);
@@ -499,7 +574,8 @@ struct PhaseMark {
 
 template <typename WsT>
 int grad_gemms(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const ChunkPtrs& c, bool first_chunk,
-               cudaStream_t s, const PhaseMark* pm = nullptr, bool last_chunk = true) {
+               cudaStream_t s, const PhaseMark* pm = nullptr, bool last_chunk = true,
+               const orda_peer_slots_t* peers = nullptr) {
   const bool tied = a->teacher_mode == ORDA_TEACHER_TIED;
   const bool sep = a->teacher_mode == ORDA_TEACHER_SEPARATE;
   void* ws_s = ws + P.off_ws_s;
@@ -554,7 +630,8 @@ int grad_gemms(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const C
       if (a->need_grad_weight) {
         const bool two = tied && P.grad_t;
         if ((r = dw_tc<WsT>(a, P, ws_s, c.hs, a->ld_student_hidden, two ? ws_t : nullptr, two ? c.ht : nullptr,
-                            a->ld_teacher_hidden, a->hidden, a->grad_weight, a->grad_weight_fp32, acc, c.rows, st, s)))
+                            a->ld_teacher_hidden, a->hidden, a->grad_weight, a->grad_weight_fp32, acc, c.rows, st, s,
+                            last_chunk ? peers : nullptr)))
           return r;
       }
       if (sep && P.grad_t && a->need_grad_teacher_weight)
@@ -618,7 +695,8 @@ int check_operands(const orda_distill_args_t* a, const Plan& P) {
 }
 
 template <typename WsT>
-int run_all(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, cudaStream_t s) {
+int run_all(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, cudaStream_t s,
+            const orda_peer_slots_t* peers = nullptr) {
   int rc;
   if (a->grads_include_mean_scale) {
     count_launch();
@@ -636,7 +714,7 @@ int run_all(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, cudaStream
     pm.mark(ORDA_PHASE_ROWS, 0);
     if ((rc = row_phases<WsT>(a, P, ws, c, s, true, true, nullptr, nullptr))) return rc;
     pm.mark(ORDA_PHASE_ROWS, 1);
-    if ((rc = grad_gemms<WsT>(a, P, ws, c, r0 == 0, s, &pm, pm.on))) return rc;
+    if ((rc = grad_gemms<WsT>(a, P, ws, c, r0 == 0, s, &pm, pm.on, peers))) return rc;
   }
   const float* rl = a->out_row_losses ? a->out_row_losses : reinterpret_cast<const float*>(ws + P.off_row_losses);
   count_launch();
@@ -707,17 +785,112 @@ int32_t orda_distill_fwdbwd(const orda_distill_args_t* args, void* workspace, si
   return dispatch_all(args, P, static_cast<uint8_t*>(workspace), static_cast<cudaStream_t>(stream));
 }
 
+// ---------------------------------------------------------------- token sharding over peer memory
+int32_t orda_distill_fwdbwd_peer(const orda_distill_args_t* args, void* workspace, size_t workspace_bytes,
+                                 const orda_peer_slots_t* peers, void* stream) {
+  int rc = check_args(args);
+  if (rc) return rc;
+  if (!peers || peers->world < 1 || peers->world > ORDA_MAX_PEERS || peers->rank < 0 || peers->rank >= peers->world)
+    return ORDA_ERR_INVALID_ARGUMENT;
+  if (args->compute_dtype == ORDA_F32 || args->grad_weight_fp32 || !args->need_grad_weight || args->vocab_offset != 0)
+    return ORDA_ERR_UNSUPPORTED;
+  if (peers->slab_rows <= 0 || peers->slab_rows * peers->world < args->vocab) return ORDA_ERR_INVALID_ARGUMENT;
+  for (int k = 0; k < peers->world; ++k)
+    if (!peers->slot_base[k] || (reinterpret_cast<uintptr_t>(peers->slot_base[k]) & 15u) != 0)
+      return ORDA_ERR_ALIGNMENT;
+  const Plan P = make_plan(args, 0);
+  if ((rc = check_operands(args, P))) return rc;
+  if (!workspace || workspace_bytes < P.total) return ORDA_ERR_WORKSPACE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  return args->compute_dtype == ORDA_BF16 ? run_all<__nv_bfloat16>(args, P, ws, s, peers)
+                                          : run_all<__half>(args, P, ws, s, peers);
+}
+
+typedef CUresult (*MemGetAddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+int32_t orda_ipc_export(const void* ptr, orda_ipc_handle_t* out) {
+  if (!ptr || !out) return ORDA_ERR_INVALID_ARGUMENT;
+  static MemGetAddressRangeFn range_fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      range_fn = reinterpret_cast<MemGetAddressRangeFn>(p);
+  });
+  if (!range_fn) return ORDA_ERR_CUDA;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range_fn(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) return ORDA_ERR_INVALID_ARGUMENT;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) return ORDA_ERR_CUDA;
+  static_assert(sizeof(h) <= sizeof(out->handle), "IPC handle size");
+  memset(out->handle, 0, sizeof(out->handle));
+  memcpy(out->handle, &h, sizeof(h));
+  out->offset = static_cast<uint64_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return ORDA_OK;
+}
+
+int32_t orda_ipc_import(const orda_ipc_handle_t* handle, void** ptr_out) {
+  if (!handle || !ptr_out) return ORDA_ERR_INVALID_ARGUMENT;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle->handle, sizeof(h));
+  void* base = nullptr;
+  if (cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return ORDA_ERR_CUDA;
+  *ptr_out = static_cast<uint8_t*>(base) + handle->offset;
+  return ORDA_OK;
+}
+
+int32_t orda_ipc_close(void* ptr, const orda_ipc_handle_t* handle) {
+  if (!ptr || !handle) return ORDA_ERR_INVALID_ARGUMENT;
+  return cudaIpcCloseMemHandle(static_cast<uint8_t*>(ptr) - handle->offset) == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
+}
+
+int32_t orda_peer_reduce_broadcast(const orda_peer_slots_t* peers, int64_t vocab, int64_t hidden, int32_t dtype,
+                                   int32_t ctas, void* stream) {
+  if (!peers || peers->world < 1 || peers->world > ORDA_MAX_PEERS || peers->rank < 0 || peers->rank >= peers->world)
+    return ORDA_ERR_INVALID_ARGUMENT;
+  if (vocab <= 0 || hidden <= 0 || peers->slab_rows <= 0 || peers->slab_rows * peers->world < vocab)
+    return ORDA_ERR_INVALID_ARGUMENT;
+  if (dtype != ORDA_BF16 && dtype != ORDA_F16) return ORDA_ERR_INVALID_ARGUMENT;
+  if (hidden % 8) return ORDA_ERR_ALIGNMENT;
+  for (int k = 0; k < peers->world; ++k)
+    if (!peers->slot_base[k] || !peers->grad_base[k] || (reinterpret_cast<uintptr_t>(peers->slot_base[k]) & 15u) ||
+        (reinterpret_cast<uintptr_t>(peers->grad_base[k]) & 15u))
+      return ORDA_ERR_ALIGNMENT;
+  const int64_t r0 = static_cast<int64_t>(peers->rank) * peers->slab_rows;
+  const int64_t rows = std::max<int64_t>(0, std::min<int64_t>(peers->slab_rows, vocab - r0));
+  if (rows == 0) return ORDA_OK;
+  PeerReduceParams q{};
+  q.world = peers->world;
+  q.rows = rows;
+  q.row0 = r0;
+  q.slab_rows = peers->slab_rows;
+  q.hidden = hidden;
+  q.slots = peers->slot_base[peers->rank];
+  for (int k = 0; k < peers->world; ++k) q.dst[k] = peers->grad_base[k];
+  const int64_t vecs = rows * (hidden / 8);
+  const int grid = static_cast<int>(std::min<int64_t>(cdiv(vecs, 256), ctas > 0 ? ctas : 2 * num_sms()));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  count_launch();
+  if (dtype == ORDA_BF16) peer_reduce_broadcast_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(q);
+  else peer_reduce_broadcast_kernel<__half><<<grid, 256, 0, s>>>(q);
+  return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
+}
+
 // ---------------------------------------------------------------- vocab-sharded phases
 size_t orda_shard_workspace_bytes(const orda_distill_args_t* args) {
   if (check_args(args) != ORDA_OK) return 0;
-  return make_plan(args, args->n_rows).total;
+  return make_plan(args, args->n_rows, false).total;
 }
 
 int32_t orda_shard_forward(const orda_distill_args_t* args, void* workspace, size_t workspace_bytes,
                            float* row_stats, void* stream) {
   int rc = check_args(args);
   if (rc) return rc;
-  const Plan P = make_plan(args, args->n_rows);
+  const Plan P = make_plan(args, args->n_rows, false);
   if ((rc = check_operands(args, P))) return rc;
   if (!workspace || workspace_bytes < P.total || !row_stats) return ORDA_ERR_WORKSPACE;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -745,7 +918,7 @@ int32_t orda_shard_jsd_partials(const orda_distill_args_t* args, void* workspace
                                 const float* row_stats, float* row_sums, void* stream) {
   int rc = check_args(args);
   if (rc) return rc;
-  const Plan P = make_plan(args, args->n_rows);
+  const Plan P = make_plan(args, args->n_rows, false);
   if (!workspace || workspace_bytes < P.total || !row_stats || !row_sums) return ORDA_ERR_WORKSPACE;
   if (!P.jsd) return ORDA_OK;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -767,7 +940,7 @@ int32_t orda_shard_backward(const orda_distill_args_t* args, void* workspace, si
                             const float* row_stats, const float* row_sums, void* stream) {
   int rc = check_args(args);
   if (rc) return rc;
-  const Plan P = make_plan(args, args->n_rows);
+  const Plan P = make_plan(args, args->n_rows, false);
   if ((rc = check_operands(args, P))) return rc;
   if (!workspace || workspace_bytes < P.total || !row_stats) return ORDA_ERR_WORKSPACE;
   if (P.jsd && !row_sums) return ORDA_ERR_INVALID_ARGUMENT;

@@ -33,6 +33,7 @@ struct RowParams {
   int64_t ld_row_losses;
   void* ws_s; void* ws_t; int64_t ld_ws;
   const void* t_gmem; int64_t ld_tg; int32_t tg_dtype;
+  int32_t tg_vec;         // teacher rows 16-byte aligned (vector loads)
   int32_t* status;
   const float* grad_scale;  // optional device scalar multiplying the dlogits (1/count for mean)
   // Column parts: each row is swept as `parts` column ranges of `part_cols` (a multiple of 256)
@@ -42,17 +43,15 @@ struct RowParams {
   int32_t parts;
   int64_t part_cols;
   float* part_records;
+  // Epilogue-statistics path (16-bit, T = 1, teacher from an accumulator or none): the logits
+  // epilogue wrote per-tile softmax sums (tile_sums, [rows][n_vtiles] float2), so the row records come
+  // from tile_merge_kernel instead of a pass over the logits. The divergence's row sums go to
+  // cross_parts ([parts][rows], JSD [2][parts][rows]): the forward-KL cross term
+  // sum_j p_t,j (u_j - z_j) from the dlogits sweep, reverse KL's R and JSD's J and G from
+  // div_sweep_kernel before it.
+  const float* tile_sums;
+  float* cross_parts;
 };
-
-constexpr float kLog2e = 1.4426950408889634f;
-
-// 2^x with the PTX ex2.approx instruction. Callers evaluate exp(x) through the identity
-// exp(x) = 2^(x * log2 e), folding the log2 e factor into the arguments they already scale.
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
 
 // Column range [c0, c1) of part `part` of a row.
 __device__ __forceinline__ void part_range(const RowParams& p, int part, int64_t& c0, int64_t& c1) {
@@ -118,8 +117,17 @@ __device__ __forceinline__ void row_loss_one(const RowParams& p, int64_t row) {
     }
     if (p.flags & F_KL) {
       const double t = p.temperature, it = p.inv_t;
-      if (p.flags & F_JSD) {
+      if (p.cross_parts && (p.flags & (F_JSD | F_KL_REVERSE))) {
+        // T = 1 reverse KL (R) or JSD (J), summed over the divergence sweep's parts
+        for (int k = 0; k < p.parts; ++k) div += (double)p.cross_parts[(int64_t)k * p.rows + row];
+      } else if (p.flags & F_JSD) {
         div = p.row_sums[row * 2] * t * t;
+      } else if (p.cross_parts) {
+        // T = 1 forward KL: sum_j p_t (u_j - z_j) - lse_t + lse_s, the cross sum from the dlogits sweep
+        double cr = 0.0;
+        for (int k = 0; k < p.parts; ++k) cr += (double)p.cross_parts[(int64_t)k * p.rows + row];
+        const double lse_t = (double)r[RS_MAX_T] + log((double)r[RS_SUM1_T]);
+        div = cr - lse_t + lse_s;
       } else {
         const double lse_st = (double)r[RS_MAX_S] * it + log((double)r[RS_SUMT_S]);
         const double lse_tt = (double)r[RS_MAX_T] * it + log((double)r[RS_SUMT_T]);
@@ -165,6 +173,32 @@ __device__ __forceinline__ void store8(T* dst, const float (&v)[8]) {
     reinterpret_cast<float4*>(dst)[0] = make_float4(v[0], v[1], v[2], v[3]);
     reinterpret_cast<float4*>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
   }
+}
+
+// Eight teacher logits [j0, j0 + 8) of a row from the caller's buffer; columns at or past `cnt` get
+// `fill`. Rows whose base and stride are 16-byte aligned (tg_vec) are read with two (fp32) or one
+// (16-bit) 16-byte loads.
+__device__ __forceinline__ float load_tg(const RowParams& p, int64_t row, int64_t col);
+__device__ __forceinline__ void load_tg8(const RowParams& p, int64_t row, int64_t j0, int cnt, float fill,
+                                         float (&u)[8]) {
+  if (cnt >= 8 && p.tg_vec) {
+    if (p.tg_dtype == ORDA_F32) {
+      const float4* q = reinterpret_cast<const float4*>(static_cast<const float*>(p.t_gmem) + row * p.ld_tg + j0);
+      const float4 a = __ldg(q), b = __ldg(q + 1);
+      u[0] = a.x; u[1] = a.y; u[2] = a.z; u[3] = a.w; u[4] = b.x; u[5] = b.y; u[6] = b.z; u[7] = b.w;
+    } else {
+      const uint4 w = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.t_gmem) + row * p.ld_tg + j0));
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (p.tg_dtype == ORDA_BF16) unpack2<__nv_bfloat16>(ws[q], u[2 * q], u[2 * q + 1]);
+        else unpack2<__half>(ws[q], u[2 * q], u[2 * q + 1]);
+      }
+    }
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) u[j] = j < cnt ? load_tg(p, row, j0 + j) : fill;
 }
 
 __device__ __forceinline__ float load_tg(const RowParams& p, int64_t row, int64_t col) {
@@ -223,16 +257,18 @@ __device__ __forceinline__ void load_row8(const RowParams& p, int64_t row, int64
   load8<WsT>(static_cast<const WsT*>(p.ws_s) + row * p.ld_ws + j0, ds);
   const float off_s = m.x - c.ms;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) ds[j] += off_s;
+  for (int j = 0; j < 8; ++j) ds[j] = fmaf(ds[j], kLn2, off_s);
   if (need_t) {
     if (p.flags & F_TEACHER_GMEM) {
+      // columns past the vocabulary read as the row maximum, i.e. offset 0 (they are never used)
+      load_tg8(p, row, j0, static_cast<int>(p.vocab - j0 < 8 ? p.vocab - j0 : 8), c.mt, dt);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) dt[j] = (j0 + j < p.vocab) ? load_tg(p, row, j0 + j) - c.mt : 0.f;
+      for (int j = 0; j < 8; ++j) dt[j] -= c.mt;
     } else {
       load8<WsT>(static_cast<const WsT*>(p.ws_t) + row * p.ld_ws + j0, dt);
       const float off_t = m.y - c.mt;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) dt[j] += off_t;
+      for (int j = 0; j < 8; ++j) dt[j] = fmaf(dt[j], kLn2, off_t);
     }
   } else {
 #pragma unroll
@@ -281,9 +317,9 @@ __global__ void __launch_bounds__(256) row_stats_kernel(RowParams p) {
     const WsT* rs = static_cast<const WsT*>(p.ws_s) + row * p.ld_ws;
     const WsT* rt = static_cast<const WsT*>(p.ws_t) + row * p.ld_ws;
     if constexpr (!TNO && TSRC != TS_GMEM) {
-      // T = 1: the tempered sums equal the plain ones. Exponents are formed in base 2 with one FMA
-      // from the stored shifted logits; the cross term is accumulated as w * (log2 difference) and
-      // converted once per lane: u - z = (tL - dL) / log2 e + (mt - Ms).
+      // T = 1: the tempered sums equal the plain ones. The stored base-2 exponents only need the
+      // per-tile offset added; the cross term is accumulated as w * (log2 difference) and converted
+      // once per lane: u - z = (tL - dL) / log2 e + (mt - Ms).
       const bool want_t = teacher && (need_t1 || kl);
       float es[2] = {0.f, 0.f}, et[2] = {0.f, 0.f}, cr[2] = {0.f, 0.f};
       for (int64_t j0 = c0 + (int64_t)lane * 8; j0 < c1; j0 += 256) {
@@ -297,18 +333,17 @@ __global__ void __launch_bounds__(256) row_stats_kernel(RowParams p) {
         for (int j = 0; j < 8; ++j) {
           const int q = j & 1;
           const bool valid = j < cnt;
-          const float dL = fmaf(ds[j], kLog2e, offs);
+          const float dL = ds[j] + offs;
           const float e = valid ? ex2_approx(dL) : 0.f;
           es[q] += e;
           if (want_t) {
-            const float tL = fmaf(dt[j], kLog2e, offt);
+            const float tL = dt[j] + offt;
             const float t = valid ? ex2_approx(tL) : 0.f;
             et[q] += t;
             if (kl) cr[q] += rev ? e * (dL - tL) : t * (tL - dL);
           }
         }
       }
-      constexpr float kLn2 = 0.6931471805599453f;
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
         s1s[q] = sts[q] = es[q];
@@ -322,8 +357,7 @@ __global__ void __launch_bounds__(256) row_stats_kernel(RowParams p) {
       load8<WsT>(rs + j0, ds);
       const int cnt = c1 - j0 < 8 ? static_cast<int>(c1 - j0) : 8;
       if constexpr (TSRC == TS_GMEM) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) u[j] = j < cnt ? load_tg(p, row, j0 + j) : -CUDART_INF_F;
+        load_tg8(p, row, j0, cnt, -CUDART_INF_F, u);
         float m8 = -CUDART_INF_F;
 #pragma unroll
         for (int j = 0; j < 8; ++j) m8 = fmaxf(m8, u[j]);
@@ -341,14 +375,14 @@ __global__ void __launch_bounds__(256) row_stats_kernel(RowParams p) {
       } else if constexpr (TSRC == TS_WS) {
         load8<WsT>(rt + j0, u);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) u[j] += m.y;  // raw teacher logit
+        for (int j = 0; j < 8; ++j) u[j] = fmaf(u[j], kLn2, m.y);  // raw teacher logit
       }
       const float off_s = m.x - Ms;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int q = j & 1;
         const bool valid = j < cnt;
-        const float d = ds[j] + off_s;  // z - M_s
+        const float d = fmaf(ds[j], kLn2, off_s);  // z - M_s
         const float e1 = valid ? __expf(d) : 0.f;
         const float et = TNO ? (valid ? __expf(d * it) : 0.f) : e1;
         s1s[q] += e1;
@@ -411,18 +445,135 @@ __global__ void __launch_bounds__(256) row_stats_kernel(RowParams p) {
   }
 }
 
-// log(exp(a) + exp(b)), stable.
-__device__ __forceinline__ float log_add_exp(float a, float b) {
-  const float m = fmaxf(a, b);
-  if (m == -CUDART_INF_F) return m;
-  return m + log1pf(__expf(-fabsf(a - b)));
+// Epilogue-statistics path, one warp per row: the row record from the per-tile maxima and softmax
+// sums the logits epilogue wrote (sum exp(z - M) = sum_tiles S_tile 2^((m_tile - M) log2 e)). Reads
+// 16 bytes per (row, tile) instead of the row's logits. T = 1, so the tempered sums are the plain
+// ones; the cross term is left to the dlogits sweep.
+__global__ void __launch_bounds__(256) tile_merge_kernel(RowParams p) {
+  const uint32_t f = p.flags;
+  const bool teacher = f & F_TEACHER;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
+  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; row < p.rows; row += warps) {
+    const float2* tm = row_tile_maxima(p, row);
+    const float2* ts = reinterpret_cast<const float2*>(p.tile_sums) + row * p.n_vtiles;
+    float ms = -CUDART_INF_F, mt = -CUDART_INF_F;
+    for (int i = lane; i < p.n_vtiles; i += 32) {
+      const float2 m = __ldg(tm + i);
+      ms = fmaxf(ms, m.x);
+      mt = fmaxf(mt, m.y);
+    }
+    ms = warp_max(ms);
+    mt = teacher ? warp_max(mt) : -CUDART_INF_F;
+    const float ms_l = ms * kLog2e, mt_l = mt * kLog2e;
+    float ss = 0.f, st = 0.f;
+    for (int i = lane; i < p.n_vtiles; i += 32) {
+      const float2 m = __ldg(tm + i);
+      const float2 e = __ldg(ts + i);
+      ss = fmaf(e.x, ex2_approx(fmaf(m.x, kLog2e, -ms_l)), ss);
+      if (teacher) st = fmaf(e.y, ex2_approx(fmaf(m.y, kLog2e, -mt_l)), st);
+    }
+    ss = warp_sum(ss);
+    st = teacher ? warp_sum(st) : 0.f;
+    if (lane == 0) {
+      float* out = p.row_stats + row * kRowStats;
+      bool ignored;
+      const int64_t ys = safe_label(p.labels[row], p.ignore_index, p.vocab_total, &ignored);
+      const bool has = !ignored && ys >= p.vocab_offset && ys < p.vocab_offset + p.vocab;
+      if (f & F_VALIDATE) {  // validate labels (debug profile): flag, never trap
+        const int64_t y = p.labels[row];
+        if (y != p.ignore_index && (y < 0 || y >= p.vocab_total)) atomicCAS(p.status, 0, ORDA_ERR_LABEL_RANGE);
+      }
+      out[RS_MAX_S] = ms;
+      out[RS_SUM1_S] = ss;
+      out[RS_SUMT_S] = ss;
+      out[RS_MAX_T] = mt;
+      out[RS_SUM1_T] = st;
+      out[RS_SUMT_T] = st;
+      out[RS_CROSS] = 0.f;
+      out[RS_LABEL_S] = has ? p.label_logits[row * 2] : 0.f;
+      out[RS_LABEL_T] = has ? p.label_logits[row * 2 + 1] : 0.f;
+      out[RS_HAS_LABEL] = has ? 1.f : 0.f;
+      out[10] = 1.f;
+      out[11] = p.inv_t;
+      for (int k = 12; k < kRowStats; ++k) out[k] = 0.f;
+    }
+  }
+}
+
+// Smallest mixture probability the JSD terms take a logarithm of (keeps 0 * log 0 at 0 where both
+// distributions underflow).
+constexpr float kTinyProb = 1e-37f;
+
+__device__ __forceinline__ float lg2_approx(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Epilogue-statistics path, T = 1, reverse KL or JSD: the per-row divergence sums that the dlogits
+// need before they can be formed, one warp per (row, column part), from the stored base-2 exponents
+// and the merged row records (log2 p = stored + per-tile constant):
+//   reverse: R = sum_j p_s,j (log p_s,j - log p_t,j) (= the row's KL(p_s || p_t))
+//   JSD:     J = sum_j [b p_t (log p_t - log m) + (1 - b) p_s (log p_s - log m)] and
+//            G = sum_j p_s g_j, g = (1 - b)(log p_s - log m), m = b p_t + (1 - b) p_s
+// Part k of row r goes to cross_parts[k * rows + r] (R or J) and, for JSD,
+// cross_parts[(parts + k) * rows + r] (G).
+template <typename WsT, int DK>
+__global__ void __launch_bounds__(256) div_sweep_kernel(RowParams p) {
+  const float beta = p.jsd_beta;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
+  const int64_t tasks = p.rows * p.parts;
+  for (int64_t task = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; task < tasks; task += warps) {
+    const int64_t row = task / p.parts;
+    const int part = static_cast<int>(task - row * p.parts);
+    int64_t c0, c1;
+    part_range(p, part, c0, c1);
+    const float2* tm = row_tile_maxima(p, row);
+    const RowConsts c = row_consts(p, row);
+    float a0 = 0.f, a1 = 0.f;
+    if (!c.ignored) {
+      const WsT* rs = static_cast<const WsT*>(p.ws_s) + row * p.ld_ws;
+      const WsT* rt = static_cast<const WsT*>(p.ws_t) + row * p.ld_ws;
+      const float base_s = -(c.ms + c.log_s1) * kLog2e, base_t = -(c.mt + c.log_t1) * kLog2e;
+      for (int64_t j0 = c0 + (int64_t)lane * 8; j0 < c1; j0 += 256) {
+        const float2 m = __ldg(tm + j0 / kVocabTile);
+        float ds[8], dt[8];
+        load8<WsT>(rs + j0, ds);
+        load8<WsT>(rt + j0, dt);
+        const float cs = fmaf(m.x, kLog2e, base_s), ct = fmaf(m.y, kLog2e, base_t);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (j0 + j >= c1) break;
+          const float lps = ds[j] + cs, lpt = dt[j] + ct;
+          const float ps = ex2_approx(lps);
+          if constexpr (DK == DK_REV) {
+            a0 = fmaf(ps, lps - lpt, a0);
+          } else {
+            const float pt = ex2_approx(lpt);
+            const float lm = lg2_approx(fmaxf(fmaf(beta, pt - ps, ps), kTinyProb));
+            const float tps = ps * (lps - lm);
+            a0 = fmaf(beta * pt, lpt - lm, fmaf(1.f - beta, tps, a0));
+            a1 += tps;
+          }
+        }
+      }
+    }
+    a0 = warp_sum(a0);
+    if (DK == DK_JSD) a1 = warp_sum(a1);
+    if (lane == 0) {
+      p.cross_parts[static_cast<int64_t>(part) * p.rows + row] = a0 * kLn2;
+      if (DK == DK_JSD) p.cross_parts[static_cast<int64_t>(p.parts + part) * p.rows + row] = a1 * (1.f - beta) * kLn2;
+    }
+  }
 }
 
 // JSD (0 < beta < 1), one warp per row: sum_j [b p_t (log p_t - log m) + (1-b) p_s (log p_s - log m)]
 // and sum_j p_s g_j with g = (1-b)(log p_s - log m); this shard's partial sums -> row_sums[row][0..1].
 template <typename WsT>
 __global__ void __launch_bounds__(256) jsd_sweep_kernel(RowParams p, float* row_sums) {
-  const float beta = p.jsd_beta, lb = logf(beta), l1b = log1pf(-beta), it = p.inv_t;
+  const float beta = p.jsd_beta, it = p.inv_t;
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
   for (int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; row < p.rows; row += warps) {
@@ -439,7 +590,7 @@ __global__ void __launch_bounds__(256) jsd_sweep_kernel(RowParams p, float* row_
           const float lps = ds[j] * it - c.log_st;
           const float lpt = dt[j] * it - c.log_tt;
           const float ps = __expf(lps), pt = __expf(lpt);
-          const float lm = log_add_exp(lb + lpt, l1b + lps);
+          const float lm = __logf(fmaxf(fmaf(beta, pt - ps, ps), kTinyProb));  // log m, m = b p_t + (1-b) p_s
           acc_j += beta * pt * (lpt - lm) + (1.f - beta) * ps * (lps - lm);
           acc_g += ps * (1.f - beta) * (lps - lm);
         }
@@ -465,27 +616,38 @@ __global__ void __launch_bounds__(256) grad_sweep_kernel(RowParams p) {
   constexpr bool kl = DK != DK_NONE;
   const bool grad_t = f & F_GRAD_T, grad_s = f & F_GRAD_S;
   const float it = p.inv_t, kls = p.w_kl * p.temperature;
-  const float beta = p.jsd_beta, lb = logf(fmaxf(beta, 1e-30f)), l1b = log1pf(-fminf(beta, 0.999999f));
+  const float beta = p.jsd_beta;
   const bool need_t = TSRC != TS_NONE && (kl || grad_t);
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
   const int64_t tasks = p.rows * p.parts;
   for (int64_t task = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; task < tasks; task += warps) {
     const int64_t row = task / p.parts;
+    const int part = static_cast<int>(task - row * p.parts);
     int64_t c0, c1;
-    part_range(p, static_cast<int>(task - row * p.parts), c0, c1);
+    part_range(p, part, c0, c1);
     const float2* tm = row_tile_maxima(p, row);
     const RowConsts c = row_consts(p, row);
     float rrev = 0.f, gsum = 0.f;
     if (DK == DK_REV) {
-      const float* r = p.row_stats + row * kRowStats;
-      rrev = r[RS_CROSS] / r[RS_SUMT_S] - c.log_st - c.ms * it + c.log_tt + c.mt * it;
+      if (p.cross_parts) {  // epilogue-statistics path: R summed over the divergence sweep's parts
+        for (int k = 0; k < p.parts; ++k) rrev += p.cross_parts[static_cast<int64_t>(k) * p.rows + row];
+      } else {
+        const float* r = p.row_stats + row * kRowStats;
+        rrev = r[RS_CROSS] / r[RS_SUMT_S] - c.log_st - c.ms * it + c.log_tt + c.mt * it;
+      }
     }
-    if (DK == DK_JSD) gsum = p.row_sums[row * 2 + 1];
+    if (DK == DK_JSD) {
+      if (p.cross_parts) {
+        for (int k = 0; k < p.parts; ++k) gsum += p.cross_parts[static_cast<int64_t>(p.parts + k) * p.rows + row];
+      } else {
+        gsum = p.row_sums[row * 2 + 1];
+      }
+    }
     const float gscale = p.grad_scale ? *p.grad_scale : 1.f;
     WsT* rs = static_cast<WsT*>(p.ws_s) + row * p.ld_ws;
     WsT* rt = static_cast<WsT*>(p.ws_t) + row * p.ld_ws;
-    if constexpr (sizeof(WsT) == 2 && !TNO && (DK == DK_FWD || DK == DK_NONE) && TSRC != TS_GMEM) {
+    if constexpr (sizeof(WsT) == 2 && !TNO && TSRC != TS_GMEM) {
       if (c.ignored) {
         const uint4 z = make_uint4(0u, 0u, 0u, 0u);
         for (int64_t j0 = c0 + (int64_t)lane * 8; j0 < c1; j0 += 256) {
@@ -494,26 +656,44 @@ __global__ void __launch_bounds__(256) grad_sweep_kernel(RowParams p) {
         }
         continue;  // next task
       }
-      // T = 1, forward KL or none: p = 2^(stored * log2 e + per-tile constant), one FMA + one ex2 per
-      // distribution; dZ_s = (w_s + w_kl) p_s - w_kl p_t - w_s [label], dZ_t = w_t (p_t - [label]),
-      // all scaled by gscale.
+      // T = 1: log2 p = stored exponent + per-tile constant, p = 2^(log2 p): one add + one ex2 per
+      // distribution. Forward KL (or none): dZ_s = (w_s + w_kl) p_s - w_kl p_t - w_s [label];
+      // reverse KL: dZ_s = w_s (p_s - [label]) + w_kl p_s (ln2 (log2 p_s - log2 p_t) - R);
+      // JSD: dZ_s = w_s (p_s - [label]) + w_kl p_s ((1 - b) ln2 (log2 p_s - log2 m) - G),
+      // m = b p_t + (1 - b) p_s. dZ_t = w_t (p_t - [label]). All scaled by gscale.
       const float kl_w = kl ? kls : 0.f;
       const float as = gscale * (p.w_s + kl_w), bs = gscale * kl_w, at = gscale * p.w_t;
       const float ys = gscale * p.w_s;
+      const float kd = gscale * kls;                 // divergence weight x T (T = 1), scaled
+      const float g_ln2 = (1.f - beta) * kLn2;       // JSD: g = (1 - b) ln2 (log2 p_s - log2 m)
       const float base_s = -(c.ms + c.log_s1) * kLog2e, base_t = -(c.mt + c.log_t1) * kLog2e;
+      // epilogue-statistics path: also sum_j p_t (u_j - z_j) for the forward-KL loss, with
+      // u - z = (stored_t - stored_s) ln 2 + (tile max_t - tile max_s)
+      const bool want_cross = DK == DK_FWD && p.cross_parts != nullptr;
+      float cross = 0.f;
       for (int64_t j0 = c0 + (int64_t)lane * 8; j0 < c1; j0 += 256) {
         const float2 m = __ldg(tm + j0 / kVocabTile);
         float ds[8], dt[8];
         load8<WsT>(rs + j0, ds);
         if (need_t) load8<WsT>(rt + j0, dt);
         const float cs = fmaf(m.x, kLog2e, base_s), ct = fmaf(m.y, kLog2e, base_t);
+        const float dm = m.y - m.x;
         float gs[8], gt[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float ps = ex2_approx(fmaf(ds[j], kLog2e, cs));
-          const float pt = need_t ? ex2_approx(fmaf(dt[j], kLog2e, ct)) : 0.f;
-          gs[j] = fmaf(as, ps, -bs * pt);
+          const float lps = ds[j] + cs, lpt = dt[j] + ct;  // base-2 log-probabilities
+          const float ps = ex2_approx(lps);
+          const float pt = need_t ? ex2_approx(lpt) : 0.f;
+          if constexpr (DK == DK_REV) {
+            gs[j] = fmaf(ys, ps, kd * ps * fmaf(lps - lpt, kLn2, -rrev));
+          } else if constexpr (DK == DK_JSD) {
+            const float lm = lg2_approx(fmaxf(fmaf(beta, pt - ps, ps), kTinyProb));
+            gs[j] = fmaf(ys, ps, kd * ps * fmaf(lps - lm, g_ln2, -gsum));
+          } else {
+            gs[j] = fmaf(as, ps, -bs * pt);
+          }
           gt[j] = at * pt;
+          if (want_cross && j0 + j < c1) cross = fmaf(pt, fmaf(dt[j] - ds[j], kLn2, dm), cross);
         }
         const int64_t lc = c.label_local - j0;  // label column inside this vector of 8
         if (lc >= 0 && lc < 8) {
@@ -536,6 +716,10 @@ __global__ void __launch_bounds__(256) grad_sweep_kernel(RowParams p) {
           u.z = pack2<WsT>(gt[4], gt[5]); u.w = pack2<WsT>(gt[6], gt[7]);
           *reinterpret_cast<uint4*>(rt + j0) = u;
         }
+      }
+      if (want_cross) {
+        cross = warp_sum(cross);
+        if (lane == 0) p.cross_parts[static_cast<int64_t>(part) * p.rows + row] = cross;
       }
     } else {
     for (int64_t j0 = c0 + (int64_t)lane * 8; j0 < c1; j0 += 256) {
@@ -560,7 +744,8 @@ __global__ void __launch_bounds__(256) grad_sweep_kernel(RowParams p) {
             const float ps = TNO ? __expf(lps) : ps1;
             float d;
             if constexpr (DK == DK_JSD) {
-              const float lm = log_add_exp(lb + lpt, l1b + lps);
+              const float pt = __expf(lpt);
+              const float lm = __logf(fmaxf(fmaf(beta, pt - ps, ps), kTinyProb));
               d = ps * ((1.f - beta) * (lps - lm) - gsum);
             } else if constexpr (DK == DK_REV) {
               d = ps * ((lps - lpt) - rrev);
@@ -700,6 +885,40 @@ __global__ void sum_split_kernel(const float* p0, const float* p1, T* out, int64
     u.w = pack2<T>(a1.z + b1.z, a1.w + b1.w);
     reinterpret_cast<uint4*>(out)[i] = u;
   }
+}
+
+// Owner side of the peer-memory gradient exchange: rows [row0, row0 + rows) of the summed gradient
+// are the sum over the `world` slots of this GPU's slot buffer ([world][slab_rows][hidden], slot k
+// written by rank k), accumulated in fp32 and rounded once, then stored into every rank's gradient
+// buffer (dst[k], peer addresses mapped here; dst[rank] is local). 16-byte vectors, grid-stride.
+struct PeerReduceParams {
+  int32_t world;
+  int64_t rows, row0, slab_rows, hidden;
+  const void* slots;
+  void* dst[ORDA_MAX_PEERS];
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256) peer_reduce_broadcast_kernel(const __grid_constant__ PeerReduceParams q) {
+  const int64_t per_row = q.hidden / 8;
+  const int64_t n = q.rows * per_row;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / per_row, c8 = i - r * per_row;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int k = 0; k < q.world; ++k) {
+      float v[8];
+      load8<T>(static_cast<const T*>(q.slots) + ((int64_t)k * q.slab_rows + r) * q.hidden + c8 * 8, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += v[j];
+    }
+    uint4 u;
+    u.x = pack2<T>(acc[0], acc[1]); u.y = pack2<T>(acc[2], acc[3]);
+    u.z = pack2<T>(acc[4], acc[5]); u.w = pack2<T>(acc[6], acc[7]);
+    const int64_t off = (q.row0 + r) * q.hidden + c8 * 8;
+    for (int k = 0; k < q.world; ++k) *reinterpret_cast<uint4*>(static_cast<T*>(q.dst[k]) + off) = u;
+  }
+  // the broadcast stores are visible system-wide once this kernel has finished
+  __threadfence_system();
 }
 
 // data *= *scale in place; every block returns at once when *scale == 1 (no memory traffic).

@@ -188,6 +188,12 @@ __device__ __forceinline__ void bulk_wait_read_all() {
 // Wait until every committed bulk store of this thread has completed.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// Orders this thread's completed async-proxy (TMA) writes to global memory before its later
+// generic-proxy accesses, and those of the threads it then synchronises with.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // Shared-memory matrix descriptor (tcgen05 "version 1" format) for a 128-byte-swizzled tile.
 //   K-major  : rows of 64 16-bit elements (128 B), 8-row swizzle atoms 1024 B apart (SBO).
 //   MN-major : 64 contiguous MN elements per 128-B row, one row per K index; 8-K-row atoms

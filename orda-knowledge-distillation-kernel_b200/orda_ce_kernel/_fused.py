@@ -39,14 +39,17 @@ _HOOKS = threading.local()
 
 
 @contextlib.contextmanager
-def instrument(phase_events=None, dweight_done_event=None, dweight_first=False, reserve_sms=0):
+def instrument(phase_events=None, dweight_done_event=None, dweight_first=False, reserve_sms=0, peer_exchange=None):
     """Attach CUDA events to the fused calls made inside the block (benchmarks / overlap):
     ``phase_events`` - 2*PHASES ``torch.cuda.Event(enable_timing=True)`` recorded around each phase;
     ``dweight_done_event`` - recorded when the weight gradients are complete;
     ``dweight_first`` - run the dW GEMMs before the dH GEMMs;
-    ``reserve_sms`` - with ``dweight_first``, SMs the dH GEMMs leave free for a concurrent all-reduce."""
+    ``reserve_sms`` - with ``dweight_first``, SMs the dH GEMMs leave free for a concurrent all-reduce;
+    ``peer_exchange`` - a :class:`orda_ce_kernel.parallel.PeerGradientExchange`: the lm_head gradient
+    is summed over the data-parallel ranks through peer memory (the returned gradient is the
+    exchange's buffer, complete once the current stream reaches it)."""
     prev = getattr(_HOOKS, "value", None)
-    _HOOKS.value = (phase_events, dweight_done_event, dweight_first, reserve_sms)
+    _HOOKS.value = (phase_events, dweight_done_event, dweight_first, reserve_sms, peer_exchange)
     try:
         yield
     finally:
@@ -261,8 +264,9 @@ def launch_prepared(pr: Prepared, spec: FusedSpec, keep_alive=None) -> None:
     lib = _native.load()
     a, dev, status = pr.args, pr.dev, pr.status
     hooks = getattr(_HOOKS, "value", None)
+    exchange = None
     if hooks is not None:
-        ev, done, first, reserve = hooks
+        ev, done, first, reserve, exchange = hooks
         if ev is not None:
             handles = (ctypes.c_void_p * (2 * _native.PHASES))(*[e.cuda_event for e in ev])
             if keep_alive is not None:
@@ -276,7 +280,13 @@ def launch_prepared(pr: Prepared, spec: FusedSpec, keep_alive=None) -> None:
     ws_bytes = int(lib.orda_distill_workspace_bytes(a))
     ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev).cuda_stream
-    _native.check(lib.orda_distill_fwdbwd(a, ws.data_ptr(), ws_bytes, stream), "orda_distill_fwdbwd")
+    if exchange is not None and pr.g_w is not None:
+        exchange.prepare(pr)
+        _native.check(lib.orda_distill_fwdbwd_peer(a, ws.data_ptr(), ws_bytes, ctypes.byref(exchange.desc), stream),
+                      "orda_distill_fwdbwd_peer")
+        exchange.complete()
+    else:
+        _native.check(lib.orda_distill_fwdbwd(a, ws.data_ptr(), ws_bytes, stream), "orda_distill_fwdbwd")
 
     if spec.validate_labels:
         code = int(status.item())

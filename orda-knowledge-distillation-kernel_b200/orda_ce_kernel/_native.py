@@ -78,6 +78,24 @@ class DistillArgs(ctypes.Structure):
     ]
 
 
+MAX_PEERS = 8
+
+
+class PeerSlots(ctypes.Structure):
+    """Mirror of orda_peer_slots_t (include/orda_b200.h)."""
+
+    _fields_ = [
+        ("world", _i32), ("rank", _i32), ("slab_rows", _i64),
+        ("slot_base", _vp * MAX_PEERS), ("grad_base", _vp * MAX_PEERS),
+    ]
+
+
+class IpcHandle(ctypes.Structure):
+    """Mirror of orda_ipc_handle_t (include/orda_b200.h)."""
+
+    _fields_ = [("handle", ctypes.c_uint8 * 64), ("offset", ctypes.c_uint64)]
+
+
 # every symbol include/orda_b200.h and include/orda_b200_testing.h declare
 EXPORTED_SYMBOLS = (
     "orda_abi_version",
@@ -87,6 +105,11 @@ EXPORTED_SYMBOLS = (
     "orda_distill_workspace_bytes",
     "orda_distill_fwdbwd",
     "orda_distill_fwdbwd_static_ws",
+    "orda_distill_fwdbwd_peer",
+    "orda_peer_reduce_broadcast",
+    "orda_ipc_export",
+    "orda_ipc_import",
+    "orda_ipc_close",
     "orda_scale_grad",
     "orda_shard_workspace_bytes",
     "orda_shard_forward",
@@ -123,6 +146,18 @@ def _declare(lib):
     lib.orda_scale_grad.argtypes = [_vp, _i64, _i32, _vp, _vp]
     lib.orda_distill_fwdbwd_static_ws.restype = _i32
     lib.orda_distill_fwdbwd_static_ws.argtypes = [P, _vp]
+    PP = ctypes.POINTER(PeerSlots)
+    lib.orda_distill_fwdbwd_peer.restype = _i32
+    lib.orda_distill_fwdbwd_peer.argtypes = [P, _vp, ctypes.c_size_t, PP, _vp]
+    lib.orda_peer_reduce_broadcast.restype = _i32
+    lib.orda_peer_reduce_broadcast.argtypes = [PP, _i64, _i64, _i32, _i32, _vp]
+    PH = ctypes.POINTER(IpcHandle)
+    lib.orda_ipc_export.restype = _i32
+    lib.orda_ipc_export.argtypes = [_vp, PH]
+    lib.orda_ipc_import.restype = _i32
+    lib.orda_ipc_import.argtypes = [PH, ctypes.POINTER(_vp)]
+    lib.orda_ipc_close.restype = _i32
+    lib.orda_ipc_close.argtypes = [_vp, PH]
     lib.orda_shard_workspace_bytes.restype = ctypes.c_size_t
     lib.orda_shard_workspace_bytes.argtypes = [P]
     lib.orda_shard_forward.restype = _i32

@@ -61,6 +61,116 @@ def token_parallel_distillation_loss(student_hidden, weight, labels, teacher, *,
     return DistillationLossOutput(loss, stats[1] * inv, stats[2] * inv, stats[3] * inv)
 
 
+class PeerGradientExchange:
+    """Sums the lm_head gradient of token-sharded data parallelism over the ranks through peer memory
+    (NVLink), instead of an NCCL all-reduce of the whole [V, H] gradient.
+
+    Rank r owns lm_head rows ``[r * slab, (r + 1) * slab)``. Two buffers per rank are mapped into every
+    peer's address space (CUDA IPC through ``orda_ipc_export`` / ``orda_ipc_import``): ``slots`` ([world * slab, H]; slot k receives rank k's
+    partial gradient of this rank's rows) and ``grad`` ([V, H], the summed gradient). Per step:
+
+    1. the fused call's dW GEMM stores each row of this rank's partial gradient into its owner's slot
+       from the GEMM epilogue (``orda_distill_fwdbwd_peer``), overlapped with the GEMM's other tiles;
+       the dHidden GEMM follows on the same stream;
+    2. on a side stream, after that GEMM: a one-element NCCL all-reduce (every rank's routed stores
+       are done), ``orda_peer_reduce_broadcast`` (this rank sums its slots and writes the sum into every
+       rank's ``grad``, beside the dHidden GEMM), and a second one-element all-reduce (every owner has
+       written this rank's ``grad``); the current stream then waits for the side stream.
+
+    No kernel waits on another GPU; the two tiny collectives order the phases. The returned lm_head
+    gradient is ``grad`` itself, reused by the next step (consume it, e.g. with the optimizer step,
+    before the next forward, as with DDP's gradient buckets).
+    """
+
+    def __init__(self, weight: torch.Tensor, group=None, reduce_ctas: int = 64):
+        import ctypes
+
+        lib = _native.load()
+        self.group = group or dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        if self.world > _native.MAX_PEERS:
+            raise ValueError(f"peer gradient exchange supports at most {_native.MAX_PEERS} ranks")
+        if weight.dtype not in (torch.bfloat16, torch.float16):
+            raise ValueError("peer gradient exchange needs a 16-bit lm_head")
+        vocab, hidden = weight.shape
+        if hidden % 8:
+            raise ValueError("peer gradient exchange needs hidden % 8 == 0")
+        dev = weight.device
+        self.vocab, self.hidden, self.dtype = vocab, hidden, weight.dtype
+        self.slab = -(-vocab // self.world)
+        self.slots = torch.empty((self.world * self.slab, hidden), dtype=weight.dtype, device=dev)
+        self.grad = torch.empty((vocab, hidden), dtype=weight.dtype, device=dev)
+        # every rank maps the other ranks' two buffers (CUDA IPC; plain peer mappings over NVLink)
+        mine = []
+        for t in (self.slots, self.grad):
+            h = _native.IpcHandle()
+            _native.check(lib.orda_ipc_export(t.data_ptr(), ctypes.byref(h)), "orda_ipc_export")
+            mine.append((bytes(h.handle), int(h.offset)))
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, mine, group=self.group)
+        d = _native.PeerSlots()
+        d.world, d.rank, d.slab_rows = self.world, self.rank, self.slab
+        self._imported = []
+        for k in range(self.world):
+            for i, (local, field) in enumerate(((self.slots, d.slot_base), (self.grad, d.grad_base))):
+                if k == self.rank:
+                    field[k] = local.data_ptr()
+                    continue
+                h = _native.IpcHandle()
+                ctypes.memmove(h.handle, everyone[k][i][0], 64)
+                h.offset = everyone[k][i][1]
+                ptr = ctypes.c_void_p()
+                _native.check(lib.orda_ipc_import(ctypes.byref(h), ctypes.byref(ptr)), "orda_ipc_import")
+                self._imported.append((ptr, h))
+                field[k] = ptr.value
+        self.desc = d
+        self.reduce_ctas = int(reduce_ctas)
+        self.comm = torch.cuda.Stream(device=dev)
+        self.dweight_done = torch.cuda.Event()
+        self.dweight_done.record()  # torch creates the CUDA event on first record; the library records it
+        self.finished = torch.cuda.Event()
+        self._flag = torch.zeros(1, dtype=torch.float32, device=dev)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers (after the last step that used them has finished)."""
+        import ctypes
+
+        if not getattr(self, "_imported", None):
+            return
+        torch.cuda.synchronize(self.grad.device)
+        lib = _native.load()
+        for ptr, h in self._imported:
+            lib.orda_ipc_close(ptr, ctypes.byref(h))
+        self._imported = []
+
+    def prepare(self, pr) -> None:
+        """Point the fused call at this exchange: its lm_head gradient is ``grad``, the dW GEMM runs
+        before the dHidden GEMM and marks its end with ``dweight_done``."""
+        if pr.g_w.shape != self.grad.shape or pr.g_w.dtype != self.grad.dtype:
+            raise ValueError("peer gradient exchange: lm_head gradient shape/dtype differs from the exchange's")
+        pr.g_w = self.grad
+        a = pr.args
+        a.grad_weight = self.grad.data_ptr()
+        a.dweight_first = 1
+        a.overlap_reserve_sms = 0
+        a.dweight_done_event = self.dweight_done.cuda_event
+
+    def complete(self) -> None:
+        """Enqueue phase 2 on the side stream after the routed dW GEMM; the current stream waits for it."""
+        lib = _native.load()
+        self.comm.wait_event(self.dweight_done)
+        with torch.cuda.stream(self.comm):
+            dist.all_reduce(self._flag, group=self.group)
+            _native.check(lib.orda_peer_reduce_broadcast(self.desc, self.vocab, self.hidden,
+                                                         _native.BF16 if self.dtype == torch.bfloat16 else _native.F16,
+                                                         self.reduce_ctas, self.comm.cuda_stream),
+                          "orda_peer_reduce_broadcast")
+            dist.all_reduce(self._flag, group=self.group)
+            self.finished.record()
+        torch.cuda.current_stream().wait_event(self.finished)
+
+
 def allreduce_weight_grad(weight: torch.Tensor, group=None, async_op: bool = False):
     """Sum ``weight.grad`` over the ranks of ``group`` (token-sharded data parallelism)."""
     if weight.grad is None:
