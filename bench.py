@@ -416,6 +416,37 @@ def run_extras(args, torch, dev, pg, world, rank, reserve, main_inputs, exchange
                                       "the in-repo float64 restatement"})
         free()
 
+    # ---- host cost of one public-API call (config 1 shape): Python validation + ctypes argument
+    # structure + the library's launch sequence, measured as the enqueue time of 50 calls
+    if world == 1 and want("host_overhead"):
+        hs1 = _dev_randn(torch, (512, 256), 11, dev, dtype=torch.float32).requires_grad_(True)
+        w1 = _dev_randn(torch, (4096, 256), 12, dev, std=0.02, dtype=torch.float32).requires_grad_(True)
+        lab1 = _dev_labels(torch, 512, 4096, 0.05, 13, dev)
+        t1 = ok.TiedTeacher(hs1.detach())
+
+        def call1():
+            out = ok.distillation_loss(hs1, w1, lab1, t1, teacher_ce_weight=0.0, kl_weight=0.0)
+            out.loss.backward()
+
+        for _ in range(5):
+            call1()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        a.record()
+        for _ in range(50):
+            call1()
+        b.record()
+        host_ms = (time.perf_counter() - t0) * 1e3 / 50
+        torch.cuda.synchronize()
+        results.append({"key": "host_overhead", "workload": "config 1 shape (N=512, H=256, V=4096, fp32), "
+                        "distillation_loss + backward, 50 calls", "host_ms_per_call": host_ms,
+                        "device_ms_per_call": a.elapsed_time(b) / 50,
+                        "note": "host_ms is the enqueue time per call (API checks, ctypes argument "
+                                "structure, launches); the device runs the calls asynchronously"})
+        del hs1, w1, lab1, t1
+        free()
+
     # ---- config 2: precomputed fp32 teacher log-probs (one GPU)
     if world == 1 and want("config2"):
         hs2 = _dev_randn(torch, (N2, H2), 21, dev).requires_grad_(True)
@@ -872,6 +903,9 @@ def run_ours(args):
     if pg is not None:
         import torch.distributed as dist
 
+        if exchange is not None:
+            exchange.close()  # every rank unmaps its peers' buffers before any rank frees its own
+        dist.barrier(group=pg)
         dist.destroy_process_group()
     return 0
 

@@ -7,7 +7,7 @@
 // tensor pipe fed from L2: the 256 x 256 kernel leaves the MMA issuer waiting for loaded stages
 // about 16% of the time.
 //
-// The accumulators are single-buffered. The epilogue drains accumulator 0 and then accumulator 1,
+// The accumulators are single-buffered. Two groups of epilogue warps drain them in parallel,
 // releasing each as soon as it is read, and the MMA issuer of the next tile waits for each one
 // separately. The logits epilogue reads each 128-column vocab tile from TMEM with all its loads in
 // flight at once, stages the shifted logits in shared memory (128-byte swizzle) and writes them with
@@ -15,7 +15,8 @@
 //
 //   warp 0 (each CTA) : TMA producer; transaction bytes of both CTAs land on the leader's barrier
 //   warp 1 (leader)   : MMA issuer
-//   warps 2..5        : epilogue of the CTA's TMEM lanes (32 per warp)
+//   warps 2..9        : epilogue; warps 2..5 drain accumulator 0 and warps 6..9 accumulator 1
+//                       (TMEM lanes 32 * (warp % 4) .. + 31 each)
 //
 // Row mapping of a tile (pair rows 0..511; CTA rank r, accumulator j, TMEM lane l):
 //   A_PLAIN      : row j*256 + r*128 + l
@@ -37,9 +38,9 @@ constexpr uint32_t kWideStagingPerWarp = 4096;                // 32 rows x 64 co
 template <int EPI>
 struct WideShape {
   static constexpr int kStages = 4;
-  // The logits epilogue runs 8 warps, 4 per accumulator, so both accumulators drain at once; the
-  // store epilogue runs 4 warps that drain accumulator 0 and then accumulator 1.
-  static constexpr int kEpiWarps = EPI == EPI_FWD_STATS ? 8 : 4;
+  // Both epilogues run 8 warps, 4 per accumulator, so the two accumulators drain at once and the
+  // part of the drain the next tile's MMAs wait for is halved.
+  static constexpr int kEpiWarps = 8;
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
   static constexpr uint32_t kStaging = EPI == EPI_FWD_STATS ? kEpiWarps * kWideStagingPerWarp : 0;
   static constexpr uint32_t kBarBytes = (2 * kStages + 4) * 8 + 16;

@@ -197,9 +197,11 @@ Plan make_plan(const orda_distill_args_t* a, int64_t chunk_override, bool allow_
   p.off_label = off; off = align256(off + sizeof(float) * 2 * p.C);
   p.off_row_stats = off; off = align256(off + sizeof(float) * kRowStats * p.C);
   p.off_row_sums = off; off = align256(off + sizeof(float) * 2 * p.C);
-  // Row sweeps split long rows into up to 4 column parts (>= 16384 columns each) so that the warp
-  // tasks spread evenly over the SMs; the parts' records are merged like vocab shards.
-  p.parts = static_cast<int32_t>(std::max<int64_t>(1, std::min<int64_t>(4, a->vocab / 16384)));
+  // Row sweeps split long rows into up to 4 column parts (>= 8192 columns each) so that the warp
+  // tasks spread evenly over the SMs and each SM has enough rows streaming at once; the parts'
+  // records are merged like vocab shards. The split depends on the vocabulary alone, so a row's
+  // arithmetic does not depend on how many rows a call has.
+  p.parts = static_cast<int32_t>(std::max<int64_t>(1, std::min<int64_t>(4, a->vocab / 8192)));
   p.part_cols = cdiv(cdiv(a->vocab, p.parts), 256) * 256;
   p.off_part_records = off;
   if (p.parts > 1) off = align256(off + sizeof(float) * kRowStats * p.parts * p.C);

@@ -133,7 +133,9 @@ class PeerGradientExchange:
         self._flag = torch.zeros(1, dtype=torch.float32, device=dev)
 
     def close(self) -> None:
-        """Unmap the peers' buffers (after the last step that used them has finished)."""
+        """Unmap the peers' buffers after the last step that used them has finished. Every rank
+        calls this, then a barrier, before any rank frees its own buffers or exits: an exporter that
+        goes away while a peer still maps its memory can stall the teardown."""
         import ctypes
 
         if not getattr(self, "_imported", None):

@@ -112,6 +112,8 @@ def _worker(rank, world, port, results):
         out[(mode, div, "peer-chunked")] = (rs, _run(mode, div, temp, d, dev, row_slice=rs, parallel="peer",
                                                      exchange=exchange, config=KernelConfig(chunk_size=64)))
     results[rank] = out
+    # every rank unmaps its peers' buffers before any rank frees its own
+    exchange.close()
     dist.barrier()
     dist.destroy_process_group()
 

@@ -452,8 +452,8 @@ def test_backward_scales_by_grad_output_and_supports_retain_graph():
 @pytest.mark.parametrize("mode", ["tied", "separate-full", "precomputed-logits"])
 @pytest.mark.parametrize("div", ["forward", "reverse", "jsd"])
 def test_row_sweeps_in_column_parts(mode, div):
-    """V >= 32768 splits each row's sweeps into column parts whose records are merged like vocab
-    shards; V = 50000 gives 3 parts with a ragged last part and labels in every part."""
+    """V >= 16384 splits each row's sweeps into column parts whose records are merged like vocab
+    shards; V = 50000 gives 4 parts with a ragged last part and labels in every part."""
     hs, weight, labels, teacher, tce, kw = _llm_inputs(mode, seed=71, BT=96, H=128, Ht=192, V=50000)
     labels[1::3] = torch.arange(labels[1::3].numel(), device=labels.device) * 997 % 50000
     if mode == "precomputed-logits":
