@@ -60,6 +60,8 @@ def _args():
     p.add_argument("--rows", type=int, default=N_TOK, help="tokens per GPU")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--chunk-size", type=int, default=0,
+                   help="rows per library chunk for the headline run (0: library default)")
     p.add_argument("--no-extras", action="store_true", help="skip the extra_workloads measurements")
     p.add_argument("--only-extras", default="", help="comma-separated extra workload keys to run (default: all)")
     p.add_argument("--dw-exchange", default="peer", choices=["peer", "nccl"],
@@ -715,6 +717,8 @@ def run_ours(args):
     labels = lab_h.to(dev)
     teacher = ok.TiedTeacher(ht)
     kw = dict(kl_weight=1.0, kl_temperature=1.0, kl_divergence=args.divergence)
+    if args.chunk_size > 0:
+        kw["config"] = ok.KernelConfig(chunk_size=args.chunk_size)
 
     comm_stream = torch.cuda.Stream(device=dev) if pg is not None else None
 
@@ -864,6 +868,11 @@ def run_ours(args):
         del phase_ev
         extras = run_extras(args, torch, dev, pg, world, rank, reserve, (hs, ht, w, labels), exchange)
 
+    vpad = -(-VOCAB // 128) * 128
+    chunk_rows = args.chunk_size if args.chunk_size > 0 else max(128, ((4 << 30) // (2 * vpad * 2)) // 128 * 128)
+    chunk_rows = min(chunk_rows, rows)
+    ws_logits = 2 * chunk_rows * vpad * 2  # student + teacher 16-bit logits of one chunk
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
@@ -879,7 +888,8 @@ def run_ours(args):
                                           if exchange is not None else "NCCL all-reduce on a side stream")
                 if world > 1 else None,
                 "overlap_reserve_sms": reserve,
-                "l2": "inputs larger than L2 (lm_head 1.05 GB, logits workspace 4.2 GB)",
+                "chunk_rows": chunk_rows,
+                "l2": f"inputs larger than L2 (lm_head 1.05 GB, logits workspace {ws_logits / 1e9:.2f} GB)",
             },
             "tflops_per_gpu": step_tf,
             "frac_of_bf16_peak_step": step_tf / peak_tf,
