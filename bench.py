@@ -869,7 +869,7 @@ def run_ours(args):
         extras = run_extras(args, torch, dev, pg, world, rank, reserve, (hs, ht, w, labels), exchange)
 
     vpad = -(-VOCAB // 128) * 128
-    chunk_rows = args.chunk_size if args.chunk_size > 0 else max(128, ((4 << 30) // (2 * vpad * 2)) // 128 * 128)
+    chunk_rows = args.chunk_size if args.chunk_size > 0 else max(128, ((2 << 30) // (2 * vpad * 2)) // 128 * 128)
     chunk_rows = min(chunk_rows, rows)
     ws_logits = 2 * chunk_rows * vpad * 2  # student + teacher 16-bit logits of one chunk
 

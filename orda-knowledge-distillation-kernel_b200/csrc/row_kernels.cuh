@@ -647,7 +647,7 @@ __global__ void __launch_bounds__(256) grad_sweep_kernel(RowParams p) {
     const float gscale = p.grad_scale ? *p.grad_scale : 1.f;
     WsT* rs = static_cast<WsT*>(p.ws_s) + row * p.ld_ws;
     WsT* rt = static_cast<WsT*>(p.ws_t) + row * p.ld_ws;
-    if constexpr (sizeof(WsT) == 2 && !TNO && TSRC != TS_GMEM) {
+    if constexpr (sizeof(WsT) == 2 && !TNO) {
       if (c.ignored) {
         const uint4 z = make_uint4(0u, 0u, 0u, 0u);
         for (int64_t j0 = c0 + (int64_t)lane * 8; j0 < c1; j0 += 256) {
@@ -675,8 +675,18 @@ __global__ void __launch_bounds__(256) grad_sweep_kernel(RowParams p) {
         const float2 m = __ldg(tm + j0 / kVocabTile);
         float ds[8], dt[8];
         load8<WsT>(rs + j0, ds);
-        if (need_t) load8<WsT>(rt + j0, dt);
-        const float cs = fmaf(m.x, kLog2e, base_s), ct = fmaf(m.y, kLog2e, base_t);
+        if (need_t) {
+          if constexpr (TSRC == TS_GMEM) {
+            // the caller's teacher logits in base 2; their constant is the row's, not a tile's
+            load_tg8(p, row, j0, static_cast<int>(p.vocab - j0 < 8 ? p.vocab - j0 : 8), 0.f, dt);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) dt[j] *= kLog2e;
+          } else {
+            load8<WsT>(rt + j0, dt);
+          }
+        }
+        const float cs = fmaf(m.x, kLog2e, base_s);
+        const float ct = TSRC == TS_GMEM ? base_t : fmaf(m.y, kLog2e, base_t);
         const float dm = m.y - m.x;
         float gs[8], gt[8];
 #pragma unroll

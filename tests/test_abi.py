@@ -67,8 +67,8 @@ def test_workspace_is_bounded_and_host_only():
     lib = _native.load()
     a = _args()
     ws = lib.orda_distill_workspace_bytes(a)
-    # two 16-bit logits chunks bounded by 4 GiB plus statistics
-    assert 0 < ws < (4 << 30) + 512 * (1 << 20)
+    # two 16-bit logits chunks bounded by 2 GiB plus statistics
+    assert 0 < ws < (2 << 30) + 512 * (1 << 20)
     a.chunk_rows = 1024
     ws_small = lib.orda_distill_workspace_bytes(a)
     assert ws_small < ws
