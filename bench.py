@@ -64,7 +64,7 @@ def _args():
                    help="rows per library chunk for the headline run (0: library default)")
     p.add_argument("--no-extras", action="store_true", help="skip the extra_workloads measurements")
     p.add_argument("--only-extras", default="", help="comma-separated extra workload keys to run (default: all)")
-    p.add_argument("--dw-exchange", default="peer", choices=["peer", "nccl"],
+    p.add_argument("--dw-exchange", default="nccl", choices=["peer", "nccl"],
                    help="N>1: sum the lm_head gradient through peer memory (fused into the dW GEMM's epilogue) "
                         "or with an NCCL all-reduce")
     p.add_argument("--reserve-sms", type=int, default=-1,

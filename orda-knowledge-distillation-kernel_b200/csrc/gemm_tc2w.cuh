@@ -397,6 +397,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WideShape<EPI>::kThr
           if (row < p.fwd.rows) lab[j] = p.fwd.labels[row];
         }
       }
+      if constexpr (EPI == EPI_STORE) {
+        // accumulating store (a later row chunk of dW): pull this lane's previous values of the tile
+        // into L2 while the MMAs still run, so the read-modify-write after the wait hits L2
+        if (p.st.accumulate) {
+          int32_t mt0, nt0, ks0, kbb0, kbc0;
+          decode(t, mt0, nt0, ks0, kbb0, kbc0);
+          const int64_t n0p = static_cast<int64_t>(nt0) * kPairBN;
+          const void* prev = p.st.peers > 0 ? p.st.acc_src : p.st.out;
+          const int64_t es = p.st.out_f32 ? 4 : 2;
+          if (prev && n0p < p.st.N) {
+            const int64_t bytes = (p.st.N - n0p < kPairBN ? p.st.N - n0p : kPairBN) * es;
+            for (int j = j_first; j <= j_last; ++j) {
+              const int64_t row = static_cast<int64_t>(mt0) * 512 + j * 256 + rank * 128 + quarter * 32 + lane;
+              if (row >= p.st.M) continue;
+              const char* base = static_cast<const char*>(prev) + (row * p.st.ldo + n0p) * es;
+              for (int64_t off = 0; off < bytes; off += 128)
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(base + off));
+            }
+          }
+        }
+      }
       const long long c0 = prof ? clk() : 0;
       if (!mbar_wait(tfull, static_cast<uint32_t>(it & 1), p.status)) break;
       const long long c1 = prof ? clk() : 0;
