@@ -114,6 +114,9 @@ struct Plan {
   // 16-bit compute, T = 1, teacher logits from an accumulator (or no teacher), gradients
   // requested, one GPU.
   bool es;
+  // Precomputed teacher logits, T = 1, JSD: the row sums come from the base-2 divergence sweep
+  // (column parts, caller's teacher logits) instead of the one-warp-per-row JSD sweep.
+  bool gmem_div;
   size_t off_tile_sums;    // [C][n_vtiles] float2
   size_t off_cross_parts;  // [parts][C] fp32
 };
@@ -183,6 +186,8 @@ Plan make_plan(const orda_distill_args_t* a, int64_t chunk_override, bool allow_
   p.flags = f;
   p.es = allow_es && epilogue_stats_enabled() && a->compute_dtype != ORDA_F32 && !p.teacher_gmem &&
          !p.t_not_one && p.any_grad;
+  p.gmem_div = allow_es && epilogue_stats_enabled() && a->compute_dtype != ORDA_F32 && p.teacher_gmem &&
+               !p.t_not_one && p.jsd;
 
   p.n_vtiles = cdiv(a->vocab, kVocabTile);
   p.vpad = p.n_vtiles * kVocabTile;
@@ -212,7 +217,7 @@ Plan make_plan(const orda_distill_args_t* a, int64_t chunk_override, bool allow_
   p.off_tile_sums = off;
   if (p.es) off = align256(off + sizeof(float) * 2 * p.C * p.n_vtiles);
   p.off_cross_parts = off;
-  if (p.es) off = align256(off + sizeof(float) * (p.jsd ? 2 : 1) * p.parts * p.C);
+  if (p.es || p.gmem_div) off = align256(off + sizeof(float) * (p.jsd ? 2 : 1) * p.parts * p.C);
   p.off_dh_split = off;
   if (a->compute_dtype != ORDA_F32 && (a->need_grad_student_hidden || a->need_grad_teacher_hidden))
     off = align256(off + sizeof(float) * 2 * p.C * std::max(a->hidden, a->teacher_hidden));
@@ -352,7 +357,7 @@ RowParams row_params(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, c
   r.part_cols = P.part_cols;
   r.part_records = reinterpret_cast<float*>(ws + P.off_part_records);
   r.tile_sums = P.es ? reinterpret_cast<const float*>(ws + P.off_tile_sums) : nullptr;
-  r.cross_parts = P.es && P.kl ? reinterpret_cast<float*>(ws + P.off_cross_parts) : nullptr;
+  r.cross_parts = (P.es && P.kl) || P.gmem_div ? reinterpret_cast<float*>(ws + P.off_cross_parts) : nullptr;
   return r;
 }
 
@@ -553,9 +558,15 @@ int row_phases(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const C
   if (!do_loss_and_sweeps) return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
   if (row_stats_ext) r.row_stats = const_cast<float*>(row_stats_ext);
   if (P.jsd && !row_sums_ext) {
-    float* sums = reinterpret_cast<float*>(ws + P.off_row_sums);
     count_launch();
-    jsd_sweep_kernel<WsT><<<row_grid, 256, 0, s>>>(r, sums);
+    bool done = false;
+    if constexpr (sizeof(WsT) == 2) {
+      if (P.gmem_div) {
+        div_sweep_kernel<WsT, DK_JSD, true><<<sweep_grid, 256, 0, s>>>(r);
+        done = true;
+      }
+    }
+    if (!done) jsd_sweep_kernel<WsT><<<row_grid, 256, 0, s>>>(r, reinterpret_cast<float*>(ws + P.off_row_sums));
   }
   if (row_sums_ext) r.row_sums = row_sums_ext;
   count_launch();

@@ -316,7 +316,59 @@ __global__ void __launch_bounds__(256) row_stats_kernel(RowParams p) {
     float s1s[2] = {0.f, 0.f}, sts[2] = {0.f, 0.f}, s1t[2] = {0.f, 0.f}, stt[2] = {0.f, 0.f}, cross[2] = {0.f, 0.f};
     const WsT* rs = static_cast<const WsT*>(p.ws_s) + row * p.ld_ws;
     const WsT* rt = static_cast<const WsT*>(p.ws_t) + row * p.ld_ws;
-    if constexpr (!TNO && TSRC != TS_GMEM) {
+    if constexpr (!TNO && TSRC == TS_GMEM) {
+      // T = 1, the caller's teacher logits: everything in base 2. The student exponents are the
+      // stored ones plus the tile offset; the teacher's are u log2 e against a per-lane running
+      // maximum (its sums and its cross term rescaled when the maximum grows). The cross term is
+      // accumulated as w * (log2 difference) and converted to natural units once per lane.
+      float es[2] = {0.f, 0.f}, et[2] = {0.f, 0.f}, cr[2] = {0.f, 0.f};
+      float mt2 = -CUDART_INF_F;
+      const float msl = Ms * kLog2e;
+      for (int64_t j0 = c0 + (int64_t)lane * 8; j0 < c1; j0 += 256) {
+        const float2 m = __ldg(tm + j0 / kVocabTile);
+        float ds[8], t2[8];
+        load8<WsT>(rs + j0, ds);
+        const int cnt = c1 - j0 < 8 ? static_cast<int>(c1 - j0) : 8;
+        load_tg8(p, row, j0, cnt, -CUDART_INF_F, t2);
+        float m8 = -CUDART_INF_F;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          t2[j] *= kLog2e;
+          m8 = fmaxf(m8, t2[j]);
+        }
+        if (m8 > mt2) {  // rescale this lane's teacher sums to the new running maximum
+          const float fac = ex2_approx(mt2 - m8);  // 0 while nothing was accumulated
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            et[q] *= fac;
+            if (!rev) cr[q] *= fac;
+          }
+          mt2 = m8;
+        }
+        const float offs = (m.x - Ms) * kLog2e;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (j >= cnt) break;
+          const int q = j & 1;
+          const float dL = ds[j] + offs;  // log2 of exp(z - Ms)
+          const float e = ex2_approx(dL);
+          const float t = ex2_approx(t2[j] - mt2);
+          es[q] += e;
+          et[q] += t;
+          if (kl) {
+            const float diff = t2[j] - (dL + msl);  // (u - z) log2 e
+            cr[q] = rev ? fmaf(-e, diff, cr[q]) : fmaf(t, diff, cr[q]);
+          }
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        s1s[q] = sts[q] = es[q];
+        s1t[q] = stt[q] = et[q];
+        cross[q] = kl ? cr[q] * kLn2 : 0.f;
+      }
+      mt = mt2 * kLn2;
+    } else if constexpr (!TNO && TSRC != TS_GMEM) {
       // T = 1: the tempered sums equal the plain ones. The stored base-2 exponents only need the
       // per-tile offset added; the cross term is accumulated as w * (log2 difference) and converted
       // once per lane: u - z = (tL - dL) / log2 e + (mt - Ms).
@@ -519,7 +571,7 @@ __device__ __forceinline__ float lg2_approx(float x) {
 //            G = sum_j p_s g_j, g = (1 - b)(log p_s - log m), m = b p_t + (1 - b) p_s
 // Part k of row r goes to cross_parts[k * rows + r] (R or J) and, for JSD,
 // cross_parts[(parts + k) * rows + r] (G).
-template <typename WsT, int DK>
+template <typename WsT, int DK, bool GMEM = false>
 __global__ void __launch_bounds__(256) div_sweep_kernel(RowParams p) {
   const float beta = p.jsd_beta;
   const int lane = threadIdx.x & 31;
@@ -541,8 +593,16 @@ __global__ void __launch_bounds__(256) div_sweep_kernel(RowParams p) {
         const float2 m = __ldg(tm + j0 / kVocabTile);
         float ds[8], dt[8];
         load8<WsT>(rs + j0, ds);
-        load8<WsT>(rt + j0, dt);
-        const float cs = fmaf(m.x, kLog2e, base_s), ct = fmaf(m.y, kLog2e, base_t);
+        if constexpr (GMEM) {
+          // the caller's teacher logits in base 2, against the row's constant
+          load_tg8(p, row, j0, static_cast<int>(c1 - j0 < 8 ? c1 - j0 : 8), 0.f, dt);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) dt[j] *= kLog2e;
+        } else {
+          load8<WsT>(rt + j0, dt);
+        }
+        const float cs = fmaf(m.x, kLog2e, base_s);
+        const float ct = GMEM ? base_t : fmaf(m.y, kLog2e, base_t);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           if (j0 + j >= c1) break;
