@@ -107,7 +107,8 @@ struct Plan {
   int32_t parts;       // column parts of the row sweeps
   int64_t part_cols;
   size_t off_part_records;
-  size_t off_dh_split;  // fp32 partials of the k-split dHidden GEMM: [2][C][max(H, Ht)]
+  int32_t dh_split;     // K (vocabulary) split of the dHidden GEMM: 4 for V >= 65536, else 2
+  size_t off_dh_split;  // fp32 partials of the k-split dHidden GEMM: [dh_split][C][max(H, Ht)]
   // Epilogue-statistics path: the logits epilogue sums each stored tile, so the row records come
   // from the tile records (no statistics pass over the logits); the divergence row sums come from
   // the dlogits sweep (forward KL) or one base-2 divergence sweep before it (reverse KL, JSD).
@@ -218,9 +219,13 @@ Plan make_plan(const orda_distill_args_t* a, int64_t chunk_override, bool allow_
   if (p.es) off = align256(off + sizeof(float) * 2 * p.C * p.n_vtiles);
   p.off_cross_parts = off;
   if (p.es || p.gmem_div) off = align256(off + sizeof(float) * (p.jsd ? 2 : 1) * p.parts * p.C);
+  // The dHidden GEMM has few output tiles (C x H), so it splits K: a 4096 x 4096 chunk has 128 wide
+  // tiles, 1.7 waves on 74 CTA pairs; a 4-way split gives 512 work units, 6.9 waves. The split
+  // depends on the vocabulary alone, so a row's arithmetic does not depend on the chunking.
+  p.dh_split = a->vocab >= 65536 ? 4 : 2;
   p.off_dh_split = off;
   if (a->compute_dtype != ORDA_F32 && (a->need_grad_student_hidden || a->need_grad_teacher_hidden))
-    off = align256(off + sizeof(float) * 2 * p.C * std::max(a->hidden, a->teacher_hidden));
+    off = align256(off + sizeof(float) * p.dh_split * p.C * std::max(a->hidden, a->teacher_hidden));
   // the fp32 path materialises raw logits, so it always needs the student (and teacher) buffer
   const bool need_s = p.write_ws_s || a->compute_dtype == ORDA_F32;
   const bool need_t = p.teacher_acc && (p.write_ws_t || a->compute_dtype == ORDA_F32);
@@ -428,9 +433,10 @@ int forward_tc(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const C
 }
 
 // dH[rows, N] = dZ[rows, V] * Wm[V, N]
-// dHidden has few output tiles (rows x H), so the wide pair kernel splits K (the vocabulary) in two:
-// each half accumulates an fp32 partial in the workspace and a sum kernel writes the 16-bit result.
-// The split does not depend on the row count, so chunking leaves every row's arithmetic unchanged.
+// dHidden has few output tiles (rows x H), so the wide pair kernel splits K (the vocabulary) into
+// P.dh_split ranges: each accumulates an fp32 partial in the workspace and a sum kernel adds them
+// in a fixed order into the 16-bit result. The split does not depend on the row count, so chunking
+// leaves every row's arithmetic unchanged.
 template <typename T16>
 int dh_tc(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const void* dz, const void* wmat, int64_t ldw,
           int64_t n, void* out, int64_t rows, int32_t* status, cudaStream_t s) {
@@ -447,8 +453,8 @@ int dh_tc(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const void* 
                                                                     reserve);
   }
   float* part = reinterpret_cast<float*>(ws + P.off_dh_split);
-  prm.ksplit = 2;
-  prm.kb_split = static_cast<int32_t>(cdiv(prm.kb0, 2));
+  prm.ksplit = P.dh_split;
+  prm.kb_split = static_cast<int32_t>(cdiv(prm.kb0, P.dh_split));
   prm.split_bytes = static_cast<int64_t>(sizeof(float)) * rows * n;
   prm.st = StoreEpiParams{part, n, rows, n, 1, 0};
   if ((rc = launch_tc2w<false, true, A_PLAIN, false, EPI_STORE, T16>(prm, cdiv(rows, 512), n, s, group_for(ROLE_DH, 4),
@@ -457,7 +463,7 @@ int dh_tc(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const void* 
   const int64_t count8 = rows * n / 8;
   count_launch();
   sum_split_kernel<T16><<<static_cast<int>(std::min<int64_t>(cdiv(count8, 256), 4 * 148)), 256, 0, s>>>(
-      part, part + rows * n, static_cast<T16*>(out), count8);
+      part, P.dh_split, rows * n, static_cast<T16*>(out), count8);
   return cudaPeekAtLastError() == cudaSuccess ? ORDA_OK : ORDA_ERR_CUDA;
 }
 

@@ -941,18 +941,24 @@ __global__ void mean_scale_kernel(const int64_t* labels, int64_t n, int64_t igno
   }
 }
 
-// out[r][c] = p0[r][c] + p1[r][c] (fp32 k-split partials of a GEMM, rows x n contiguous) in the 16-bit
+// out[r][c] = sum_k part[k][r][c] over the `splits` fp32 k-split partials of a GEMM (each rows x n
+// contiguous, `stride` elements apart), added in order k = 0, 1, ... and rounded once to the 16-bit
 // output type; n is a multiple of 8.
 template <typename T>
-__global__ void sum_split_kernel(const float* p0, const float* p1, T* out, int64_t count8) {
+__global__ void sum_split_kernel(const float* part, int splits, int64_t stride, T* out, int64_t count8) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count8; i += (int64_t)gridDim.x * blockDim.x) {
-    const float4 a0 = reinterpret_cast<const float4*>(p0)[2 * i], a1 = reinterpret_cast<const float4*>(p0)[2 * i + 1];
-    const float4 b0 = reinterpret_cast<const float4*>(p1)[2 * i], b1 = reinterpret_cast<const float4*>(p1)[2 * i + 1];
+    float4 a0 = reinterpret_cast<const float4*>(part)[2 * i], a1 = reinterpret_cast<const float4*>(part)[2 * i + 1];
+    for (int k = 1; k < splits; ++k) {
+      const float4* q = reinterpret_cast<const float4*>(part + k * stride);
+      const float4 b0 = q[2 * i], b1 = q[2 * i + 1];
+      a0.x += b0.x; a0.y += b0.y; a0.z += b0.z; a0.w += b0.w;
+      a1.x += b1.x; a1.y += b1.y; a1.z += b1.z; a1.w += b1.w;
+    }
     uint4 u;
-    u.x = pack2<T>(a0.x + b0.x, a0.y + b0.y);
-    u.y = pack2<T>(a0.z + b0.z, a0.w + b0.w);
-    u.z = pack2<T>(a1.x + b1.x, a1.y + b1.y);
-    u.w = pack2<T>(a1.z + b1.z, a1.w + b1.w);
+    u.x = pack2<T>(a0.x, a0.y);
+    u.y = pack2<T>(a0.z, a0.w);
+    u.z = pack2<T>(a1.x, a1.y);
+    u.w = pack2<T>(a1.z, a1.w);
     reinterpret_cast<uint4*>(out)[i] = u;
   }
 }
