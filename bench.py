@@ -803,7 +803,7 @@ def run_ours(args):
                 for p in range(_native.PHASES)]
     flops_tok = {0: 4.0 * HID * VOCAB, 2: 2.0 * HID * VOCAB, 3: 4.0 * HID * VOCAB}  # fwd (s+t), dH_s, dW (s+t)
     names = {0: "logits GEMM + statistics epilogue (tc2w_gemm_kernel, 512x256 pair tiles)", 1: "row kernels",
-             2: "dHidden GEMM (tc2w_gemm_kernel, K split in two)", 3: "dWeight GEMM (tc2w_gemm_kernel)"}
+             2: "dHidden GEMM (tc2w_gemm_kernel, K split 4 ways)", 3: "dWeight GEMM (tc2w_gemm_kernel)"}
     dom = max((0, 2, 3), key=lambda p: phase_ms[p])
     peak_tf, peak_sus, peak_hbm, peak_src = _peaks()
     achieved = flops_tok[dom] * last_rows / (phase_ms[dom] / 1e3) / 1e12
