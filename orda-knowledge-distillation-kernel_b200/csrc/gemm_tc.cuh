@@ -118,111 +118,63 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t base, int kk) {
   else return smem_desc_sw128(base + kk * 32u, 16u, 1024u);
 }
 
-// Destination of 32 columns [col0, col0 + 32) of row `row` in the 16-bit output, and where the
-// previous value to accumulate comes from (routed rows read the local partial in acc_src).
-template <typename T16>
-__device__ __forceinline__ void store_target(const StoreEpiParams& st, int64_t row, int64_t col0, T16*& o,
-                                             const T16*& prev_src) {
-  if (st.peers > 0) {
-    const int64_t owner = row / st.slab_rows;
-    o = static_cast<T16*>(st.peer_base[owner]) + (st.slot * st.slab_rows + row - owner * st.slab_rows) * st.ldo + col0;
-    prev_src = st.acc_src ? static_cast<const T16*>(st.acc_src) + row * st.ldo + col0 : nullptr;
-  } else {
-    o = static_cast<T16*>(st.out) + row * st.ldo + col0;
-    prev_src = o;
-  }
-}
-
-// Writes 32 accumulator columns of one row (general path: fp32 output, ragged edges, strides that
-// are not 16-byte multiples).
-template <typename T16>
-__device__ __forceinline__ void store_cols_general(const StoreEpiParams& st, int64_t row, int64_t col0, float (&v)[32]) {
-  const int cnt = static_cast<int>((st.N - col0 < 32 ? st.N - col0 : (int64_t)32));
-  if (st.out_f32) {
-    float* o = static_cast<float*>(st.out) + row * st.ldo + col0;
-    if (cnt == 32 && (st.ldo % 4) == 0) {
-      float4* o4 = reinterpret_cast<float4*>(o);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float4 a = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-        if (st.accumulate) {
-          const float4 b = o4[j];
-          a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
-        }
-        o4[j] = a;
-      }
-    } else {
-      for (int j = 0; j < cnt; ++j) o[j] = st.accumulate ? o[j] + v[j] : v[j];
-    }
-  } else {
-    T16* o;
-    const T16* prev_src;
-    store_target<T16>(st, row, col0, o, prev_src);
-    for (int j = 0; j < cnt; ++j) {
-      const float prev = st.accumulate && prev_src ? Conv<T16>::to_f(prev_src[j]) : 0.f;
-      o[j] = Conv<T16>::from_f(prev + v[j]);
-    }
-  }
-}
-
-// Store epilogue of one accumulator row (one TMEM lane per thread), bn columns from n0. Columns go
-// out 64 at a time: both 32-column TMEM loads (and, when accumulating, the previous 16-bit values)
-// are in flight before the first wait, which halves the serialized TMEM round trips of the drain.
 template <typename T16>
 __device__ __forceinline__ void store_epilogue(const StoreEpiParams& st, uint32_t tbase, int64_t row, int64_t n0,
                                                int bn) {
   const bool row_ok = row < st.M;
-  const bool fast16 = !st.out_f32 && (st.ldo % 8) == 0;
 #pragma unroll 1
-  for (int c = 0; c < bn / 32; c += 2) {
-    const bool two = c + 1 < bn / 32;
-    uint32_t r[2][32];
-    // previous values of both 32-column groups (16-bit fast path), loaded before the TMEM wait
-    uint4 prev[2][4];
-    bool have_prev[2] = {false, false};
-    if (row_ok && fast16 && st.accumulate) {
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int64_t col0 = n0 + (c + h) * 32;
-        if ((h == 0 || two) && col0 + 32 <= st.N) {
-          T16* o;
-          const T16* prev_src;
-          store_target<T16>(st, row, col0, o, prev_src);
-          if (prev_src) {
-            const uint4* i4 = reinterpret_cast<const uint4*>(prev_src);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) prev[h][q] = i4[q];
-            have_prev[h] = true;
-          }
-        }
-      }
-    }
-    tmem_ld32_async(tbase + c * 32, r[0]);
-    if (two) tmem_ld32_async(tbase + (c + 1) * 32, r[1]);
-    tmem_wait_ld();
+  for (int c = 0; c < bn / 32; ++c) {
+    float v[32];
+    tmem_ld32(tbase + c * 32, v);
     if (!row_ok) continue;
+    const int64_t col0 = n0 + c * 32;
+    if (col0 >= st.N) continue;
+    const int cnt = static_cast<int>((st.N - col0 < 32 ? st.N - col0 : (int64_t)32));
+    if (st.out_f32) {
+      float* o = static_cast<float*>(st.out) + row * st.ldo + col0;
+      if (cnt == 32 && (st.ldo % 4) == 0) {
+        float4* o4 = reinterpret_cast<float4*>(o);
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int64_t col0 = n0 + (c + h) * 32;
-      if ((h == 1 && !two) || col0 >= st.N) continue;
-      float v[32];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[h][j]);
-      if (fast16 && col0 + 32 <= st.N) {
-        T16* o;
-        const T16* prev_src;
-        store_target<T16>(st, row, col0, o, prev_src);
-        if (have_prev[h]) {
+        for (int j = 0; j < 8; ++j) {
+          float4 a = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          if (st.accumulate) {
+            const float4 b = o4[j];
+            a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+          }
+          o4[j] = a;
+        }
+      } else {
+        for (int j = 0; j < cnt; ++j) o[j] = st.accumulate ? o[j] + v[j] : v[j];
+      }
+    } else {
+      T16* o;
+      const T16* prev_src;
+      if (st.peers > 0) {
+        const int64_t owner = row / st.slab_rows;
+        o = static_cast<T16*>(st.peer_base[owner]) + (st.slot * st.slab_rows + row - owner * st.slab_rows) * st.ldo +
+            col0;
+        prev_src = st.acc_src ? static_cast<const T16*>(st.acc_src) + row * st.ldo + col0 : nullptr;
+      } else {
+        o = static_cast<T16*>(st.out) + row * st.ldo + col0;
+        prev_src = o;
+      }
+      if (cnt == 32 && (st.ldo % 8) == 0) {
+        if (st.accumulate && prev_src) {
+          const uint4* i4 = reinterpret_cast<const uint4*>(prev_src);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            const T16* bh = reinterpret_cast<const T16*>(&prev[h][q]);
+            const uint4 b = i4[q];
+            const T16* bh = reinterpret_cast<const T16*>(&b);
 #pragma unroll
             for (int j = 0; j < 8; ++j) v[8 * q + j] += Conv<T16>::to_f(bh[j]);
           }
         }
         store_chunk32<T16>(o, v);
       } else {
-        store_cols_general<T16>(st, row, col0, v);
+        for (int j = 0; j < cnt; ++j) {
+          const float prev = st.accumulate && prev_src ? Conv<T16>::to_f(prev_src[j]) : 0.f;
+          o[j] = Conv<T16>::from_f(prev + v[j]);
+        }
       }
     }
   }
