@@ -290,7 +290,7 @@ enum DivKind { DK_NONE = 0, DK_FWD = 1, DK_REV = 2, DK_JSD = 3 };
 // row is normalised on the fly (running maximum, rescaled sums). Each lane keeps two sets of
 // accumulators (even / odd columns) to shorten the dependency chains.
 template <typename WsT, int TSRC, bool TNO>
-__global__ void __launch_bounds__(256) row_stats_kernel(RowParams p) {
+__global__ void __launch_bounds__(256, 4) row_stats_kernel(RowParams p) {
   const uint32_t f = p.flags;
   constexpr bool teacher = TSRC != TS_NONE;
   const bool need_t1 = f & F_TEACHER_CE, kl = f & F_KL, rev = f & F_KL_REVERSE;
@@ -572,7 +572,7 @@ __device__ __forceinline__ float lg2_approx(float x) {
 // Part k of row r goes to cross_parts[k * rows + r] (R or J) and, for JSD,
 // cross_parts[(parts + k) * rows + r] (G).
 template <typename WsT, int DK, bool GMEM = false>
-__global__ void __launch_bounds__(256) div_sweep_kernel(RowParams p) {
+__global__ void __launch_bounds__(256, 4) div_sweep_kernel(RowParams p) {
   const float beta = p.jsd_beta;
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
@@ -632,7 +632,7 @@ __global__ void __launch_bounds__(256) div_sweep_kernel(RowParams p) {
 // JSD (0 < beta < 1), one warp per row: sum_j [b p_t (log p_t - log m) + (1-b) p_s (log p_s - log m)]
 // and sum_j p_s g_j with g = (1-b)(log p_s - log m); this shard's partial sums -> row_sums[row][0..1].
 template <typename WsT>
-__global__ void __launch_bounds__(256) jsd_sweep_kernel(RowParams p, float* row_sums) {
+__global__ void __launch_bounds__(256, 4) jsd_sweep_kernel(RowParams p, float* row_sums) {
   const float beta = p.jsd_beta, it = p.inv_t;
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
@@ -671,7 +671,7 @@ __global__ void __launch_bounds__(256) jsd_sweep_kernel(RowParams p, float* row_
 // Teacher (teacher CE only; the divergence never reaches the teacher): w_t (softmax(u) - onehot).
 // Ignored rows are zeroed.
 template <typename WsT, int TSRC, int DK, bool TNO>
-__global__ void __launch_bounds__(256) grad_sweep_kernel(RowParams p) {
+__global__ void __launch_bounds__(256, 4) grad_sweep_kernel(RowParams p) {
   const uint32_t f = p.flags;
   constexpr bool kl = DK != DK_NONE;
   const bool grad_t = f & F_GRAD_T, grad_s = f & F_GRAD_S;
