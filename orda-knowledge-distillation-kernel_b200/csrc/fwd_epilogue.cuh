@@ -35,9 +35,11 @@ struct FwdEpiParams {
   int32_t tg_dtype;
   float* tile_stats;              // [rows][n_vtiles][kTileStats]
   float* label_logits;            // [rows][2]
-  // Optional ([rows][n_vtiles] float2 {student, teacher}): per (row, vocab tile) sum of 2^y over the
-  // tile's stored base-2 exponents y, i.e. sum exp(z - m_tile). The wide GEMM's epilogue forms it
-  // after releasing the accumulator, from the tile it has just stored.
+  // Optional: per (row, vocab tile) sum of 2^y over the tile's stored base-2 exponents y, i.e.
+  // sum exp(z - m_tile), as [rows][n_vtiles] float2 {student, teacher}; at T != 1 (F_T_NOT_ONE) also
+  // the tempered sum exp((z - m_tile) / T), as float4 {student, student tempered, teacher, teacher
+  // tempered}. The wide GEMM's epilogue forms it after releasing the accumulator, from the tile it
+  // has just stored.
   float* tile_sums;
   int32_t plain_teacher;          // wide kernel, A_PLAIN: the accumulators hold teacher logits
 };

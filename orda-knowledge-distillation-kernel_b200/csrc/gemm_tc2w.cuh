@@ -141,7 +141,7 @@ __device__ __forceinline__ void wide_fwd_acc(const FwdEpiParams& p, const CUtens
 
 // Softmax sums of the vocab tiles [n0, n0 + 256) of one row, read back from the workspace after this
 // warp's TMA stores of them have completed: per 128-column tile, sum 2^y over its valid columns (the
-// stored base-2 exponents relative to the tile maximum). Runs after the accumulator has been released,
+// stored base-2 exponents relative to the tile maximum) and, at a temperature T != 1, sum 2^(y / T). Runs after the accumulator has been released,
 // so its ex2 work overlaps the next tile's MMAs instead of delaying them. Every lane reads its own
 // row (16-byte vectors through L2, where the stores have just landed).
 template <typename WsT>
@@ -150,13 +150,15 @@ __device__ __forceinline__ void wide_tile_sums(const FwdEpiParams& p, int64_t ro
   const WsT* src = static_cast<const WsT*>(student ? p.ws_s : p.ws_t) + row * p.ld_ws + n0;
   const int tile0 = static_cast<int>(n0 / kVocabTile);
   const int ntiles = p.n_vtiles - tile0 < 2 ? p.n_vtiles - tile0 : 2;
+  const bool tempered = (p.flags & F_T_NOT_ONE) != 0;  // also sum 2^(y / T) for the tempered softmax
+  const float it = p.inv_t;
   for (int h = 0; h < ntiles; ++h) {
     const int64_t nh = n0 + h * kVocabTile;
     const int nvalid = static_cast<int>(p.vocab - nh < kVocabTile ? p.vocab - nh : kVocabTile);
     uint4 v[16];
 #pragma unroll
     for (int k = 0; k < 16; ++k) v[k] = __ldcg(reinterpret_cast<const uint4*>(src + h * kVocabTile) + k);
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    float acc[4] = {0.f, 0.f, 0.f, 0.f}, accT[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int k = 0; k < 16; ++k) {
       const uint32_t w[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
@@ -165,14 +167,19 @@ __device__ __forceinline__ void wide_tile_sums(const FwdEpiParams& p, int64_t ro
         float a, b;
         unpack2<WsT>(w[q], a, b);
         const int col = k * 8 + q * 2;
-        if (nvalid == kVocabTile) {
-          acc[q] += ex2_approx(a) + ex2_approx(b);
-        } else {
-          acc[q] += (col < nvalid ? ex2_approx(a) : 0.f) + (col + 1 < nvalid ? ex2_approx(b) : 0.f);
-        }
+        const bool va = nvalid == kVocabTile || col < nvalid, vb = nvalid == kVocabTile || col + 1 < nvalid;
+        acc[q] += (va ? ex2_approx(a) : 0.f) + (vb ? ex2_approx(b) : 0.f);
+        if (tempered) accT[q] += (va ? ex2_approx(a * it) : 0.f) + (vb ? ex2_approx(b * it) : 0.f);
       }
     }
-    p.tile_sums[(row * p.n_vtiles + tile0 + h) * 2 + (student ? 0 : 1)] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+    const float s1 = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+    if (tempered) {
+      float* rec = p.tile_sums + (row * p.n_vtiles + tile0 + h) * 4 + (student ? 0 : 2);
+      rec[0] = s1;
+      rec[1] = (accT[0] + accT[1]) + (accT[2] + accT[3]);
+    } else {
+      p.tile_sums[(row * p.n_vtiles + tile0 + h) * 2 + (student ? 0 : 1)] = s1;
+    }
   }
 }
 

@@ -118,12 +118,22 @@ struct Plan {
   // Precomputed teacher logits, T = 1, JSD: the row sums come from the base-2 divergence sweep
   // (column parts, caller's teacher logits) instead of the one-warp-per-row JSD sweep.
   bool gmem_div;
-  size_t off_tile_sums;    // [C][n_vtiles] float2
+  size_t off_tile_sums;    // [C][n_vtiles] float2 (T = 1) or float4 (T != 1: plain and tempered sums)
   size_t off_cross_parts;  // [parts][C] fp32
 };
 
 // ORDA_EPILOGUE_STATS=0 turns the epilogue-statistics path off (A/B measurements and tests of the
 // statistics-pass path on the same inputs).
+// The epilogue-statistics path at T != 1 (tempered tile sums, tempered divergence sweeps): on while
+// ORDA_EPILOGUE_STATS_T=1, until it is the default.
+bool epilogue_stats_tempered() {
+  static const bool on = [] {
+    const char* e = getenv("ORDA_EPILOGUE_STATS_T");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+
 bool epilogue_stats_enabled() {
   static const bool on = [] {
     const char* e = getenv("ORDA_EPILOGUE_STATS");
@@ -186,7 +196,7 @@ Plan make_plan(const orda_distill_args_t* a, int64_t chunk_override, bool allow_
   if (a->validate_labels) f |= F_VALIDATE;
   p.flags = f;
   p.es = allow_es && epilogue_stats_enabled() && a->compute_dtype != ORDA_F32 && !p.teacher_gmem &&
-         !p.t_not_one && p.any_grad;
+         (!p.t_not_one || epilogue_stats_tempered()) && p.any_grad;
   p.gmem_div = allow_es && epilogue_stats_enabled() && a->compute_dtype != ORDA_F32 && p.teacher_gmem &&
                !p.t_not_one && p.jsd;
 
@@ -216,7 +226,7 @@ Plan make_plan(const orda_distill_args_t* a, int64_t chunk_override, bool allow_
   p.off_part_records = off;
   if (p.parts > 1) off = align256(off + sizeof(float) * kRowStats * p.parts * p.C);
   p.off_tile_sums = off;
-  if (p.es) off = align256(off + sizeof(float) * 2 * p.C * p.n_vtiles);
+  if (p.es) off = align256(off + sizeof(float) * (p.t_not_one ? 4 : 2) * p.C * p.n_vtiles);
   p.off_cross_parts = off;
   if (p.es || p.gmem_div) off = align256(off + sizeof(float) * (p.jsd ? 2 : 1) * p.parts * p.C);
   // The dHidden GEMM has few output tiles (C x H), so it splits K: a 4096 x 4096 chunk has 128 wide

@@ -117,9 +117,11 @@ __device__ __forceinline__ void row_loss_one(const RowParams& p, int64_t row) {
     }
     if (p.flags & F_KL) {
       const double t = p.temperature, it = p.inv_t;
-      if (p.cross_parts && (p.flags & (F_JSD | F_KL_REVERSE))) {
-        // T = 1 reverse KL (R) or JSD (J), summed over the divergence sweep's parts
+      if (p.cross_parts && (p.flags & (F_JSD | F_KL_REVERSE | F_T_NOT_ONE))) {
+        // reverse KL (R), JSD (J), or at T != 1 forward KL, of the tempered distributions, summed
+        // over the sweeps' parts
         for (int k = 0; k < p.parts; ++k) div += (double)p.cross_parts[(int64_t)k * p.rows + row];
+        div *= t * t;
       } else if (p.flags & F_JSD) {
         div = p.row_sums[row * 2] * t * t;
       } else if (p.cross_parts) {
@@ -498,17 +500,18 @@ __global__ void __launch_bounds__(256, 4) row_stats_kernel(RowParams p) {
 }
 
 // Epilogue-statistics path, one warp per row: the row record from the per-tile maxima and softmax
-// sums the logits epilogue wrote (sum exp(z - M) = sum_tiles S_tile 2^((m_tile - M) log2 e)). Reads
-// 16 bytes per (row, tile) instead of the row's logits. T = 1, so the tempered sums are the plain
-// ones; the cross term is left to the dlogits sweep.
+// sums the logits epilogue wrote (sum exp(z - M) = sum_tiles S_tile 2^((m_tile - M) log2 e), and at
+// T != 1 the tempered sums with the offsets divided by T). Reads 16 to 24 bytes per (row, tile)
+// instead of the row's logits. The divergence's row sums are left to the sweeps.
 __global__ void __launch_bounds__(256) tile_merge_kernel(RowParams p) {
   const uint32_t f = p.flags;
   const bool teacher = f & F_TEACHER;
+  const bool tempered = f & F_T_NOT_ONE;
+  const float it = p.inv_t;
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
   for (int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; row < p.rows; row += warps) {
     const float2* tm = row_tile_maxima(p, row);
-    const float2* ts = reinterpret_cast<const float2*>(p.tile_sums) + row * p.n_vtiles;
     float ms = -CUDART_INF_F, mt = -CUDART_INF_F;
     for (int i = lane; i < p.n_vtiles; i += 32) {
       const float2 m = __ldg(tm + i);
@@ -518,15 +521,33 @@ __global__ void __launch_bounds__(256) tile_merge_kernel(RowParams p) {
     ms = warp_max(ms);
     mt = teacher ? warp_max(mt) : -CUDART_INF_F;
     const float ms_l = ms * kLog2e, mt_l = mt * kLog2e;
-    float ss = 0.f, st = 0.f;
+    float ss = 0.f, st = 0.f, sst = 0.f, stt = 0.f;
     for (int i = lane; i < p.n_vtiles; i += 32) {
       const float2 m = __ldg(tm + i);
-      const float2 e = __ldg(ts + i);
-      ss = fmaf(e.x, ex2_approx(fmaf(m.x, kLog2e, -ms_l)), ss);
-      if (teacher) st = fmaf(e.y, ex2_approx(fmaf(m.y, kLog2e, -mt_l)), st);
+      const float ds = fmaf(m.x, kLog2e, -ms_l), dt = fmaf(m.y, kLog2e, -mt_l);  // tile offsets, base 2
+      if (tempered) {
+        const float4 e = __ldg(reinterpret_cast<const float4*>(p.tile_sums) + row * p.n_vtiles + i);
+        ss = fmaf(e.x, ex2_approx(ds), ss);
+        sst = fmaf(e.y, ex2_approx(ds * it), sst);
+        if (teacher) {
+          st = fmaf(e.z, ex2_approx(dt), st);
+          stt = fmaf(e.w, ex2_approx(dt * it), stt);
+        }
+      } else {
+        const float2 e = __ldg(reinterpret_cast<const float2*>(p.tile_sums) + row * p.n_vtiles + i);
+        ss = fmaf(e.x, ex2_approx(ds), ss);
+        if (teacher) st = fmaf(e.y, ex2_approx(dt), st);
+      }
     }
     ss = warp_sum(ss);
     st = teacher ? warp_sum(st) : 0.f;
+    if (tempered) {
+      sst = warp_sum(sst);
+      stt = teacher ? warp_sum(stt) : 0.f;
+    } else {
+      sst = ss;
+      stt = st;
+    }
     if (lane == 0) {
       float* out = p.row_stats + row * kRowStats;
       bool ignored;
@@ -538,10 +559,10 @@ __global__ void __launch_bounds__(256) tile_merge_kernel(RowParams p) {
       }
       out[RS_MAX_S] = ms;
       out[RS_SUM1_S] = ss;
-      out[RS_SUMT_S] = ss;
+      out[RS_SUMT_S] = sst;
       out[RS_MAX_T] = mt;
       out[RS_SUM1_T] = st;
-      out[RS_SUMT_T] = st;
+      out[RS_SUMT_T] = stt;
       out[RS_CROSS] = 0.f;
       out[RS_LABEL_S] = has ? p.label_logits[row * 2] : 0.f;
       out[RS_LABEL_T] = has ? p.label_logits[row * 2 + 1] : 0.f;
@@ -563,9 +584,10 @@ __device__ __forceinline__ float lg2_approx(float x) {
   return y;
 }
 
-// Epilogue-statistics path, T = 1, reverse KL or JSD: the per-row divergence sums that the dlogits
-// need before they can be formed, one warp per (row, column part), from the stored base-2 exponents
-// and the merged row records (log2 p = stored + per-tile constant):
+// Epilogue-statistics path (and precomputed teacher logits at T = 1, JSD), reverse KL or JSD: the
+// per-row divergence sums that the dlogits need before they can be formed, one warp per (row, column
+// part), from the stored base-2 exponents and the merged row records, with the tempered
+// distributions p = softmax(z / T) (log2 p = stored / T + per-tile constant):
 //   reverse: R = sum_j p_s,j (log p_s,j - log p_t,j) (= the row's KL(p_s || p_t))
 //   JSD:     J = sum_j [b p_t (log p_t - log m) + (1 - b) p_s (log p_s - log m)] and
 //            G = sum_j p_s g_j, g = (1 - b)(log p_s - log m), m = b p_t + (1 - b) p_s
@@ -588,7 +610,10 @@ __global__ void __launch_bounds__(256, 4) div_sweep_kernel(RowParams p) {
     if (!c.ignored) {
       const WsT* rs = static_cast<const WsT*>(p.ws_s) + row * p.ld_ws;
       const WsT* rt = static_cast<const WsT*>(p.ws_t) + row * p.ld_ws;
-      const float base_s = -(c.ms + c.log_s1) * kLog2e, base_t = -(c.mt + c.log_t1) * kLog2e;
+      // tempered base-2 log-probabilities: log2 p^T = (z log2 e) / T - (M / T + log S_T) log2 e, with
+      // z log2 e = stored exponent + tile maximum * log2 e (T = 1: the plain ones)
+      const float it = p.inv_t, itl = it * kLog2e;
+      const float base_s = -(c.ms * it + c.log_st) * kLog2e, base_t = -(c.mt * it + c.log_tt) * kLog2e;
       for (int64_t j0 = c0 + (int64_t)lane * 8; j0 < c1; j0 += 256) {
         const float2 m = __ldg(tm + j0 / kVocabTile);
         float ds[8], dt[8];
@@ -601,12 +626,12 @@ __global__ void __launch_bounds__(256, 4) div_sweep_kernel(RowParams p) {
         } else {
           load8<WsT>(rt + j0, dt);
         }
-        const float cs = fmaf(m.x, kLog2e, base_s);
-        const float ct = GMEM ? base_t : fmaf(m.y, kLog2e, base_t);
+        const float cs = fmaf(m.x, itl, base_s);
+        const float ct = GMEM ? base_t : fmaf(m.y, itl, base_t);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           if (j0 + j >= c1) break;
-          const float lps = ds[j] + cs, lpt = dt[j] + ct;
+          const float lps = fmaf(ds[j], it, cs), lpt = fmaf(dt[j], it, ct);
           const float ps = ex2_approx(lps);
           if constexpr (DK == DK_REV) {
             a0 = fmaf(ps, lps - lpt, a0);
@@ -792,6 +817,10 @@ __global__ void __launch_bounds__(256, 4) grad_sweep_kernel(RowParams p) {
         if (lane == 0) p.cross_parts[static_cast<int64_t>(part) * p.rows + row] = cross;
       }
     } else {
+    // epilogue-statistics path at T != 1, forward KL: this part's sum_j p_t (log p_t - log p_s) of
+    // the tempered distributions, for the row loss
+    const bool want_kl = DK == DK_FWD && p.cross_parts != nullptr;
+    float klsum = 0.f;
     for (int64_t j0 = c0 + (int64_t)lane * 8; j0 < c1; j0 += 256) {
       float gs[8], gt[8];
       if (c.ignored) {
@@ -826,6 +855,7 @@ __global__ void __launch_bounds__(256, 4) grad_sweep_kernel(RowParams p) {
                 have_pt1 = true;
               }
               d = ps - pt;
+              if (want_kl && j0 + j < c1) klsum = fmaf(pt, lpt - lps, klsum);
             }
             g += kls * d;
           }
@@ -840,6 +870,10 @@ __global__ void __launch_bounds__(256, 4) grad_sweep_kernel(RowParams p) {
       }
       if (grad_s) store8<WsT>(rs + j0, gs);
       if (grad_t) store8<WsT>(rt + j0, gt);
+    }
+    if (want_kl) {
+      klsum = warp_sum(klsum);
+      if (lane == 0) p.cross_parts[static_cast<int64_t>(part) * p.rows + row] = klsum;
     }
     }
   }
