@@ -112,8 +112,8 @@ struct Plan {
   // Epilogue-statistics path: the logits epilogue sums each stored tile, so the row records come
   // from the tile records (no statistics pass over the logits); the divergence row sums come from
   // the dlogits sweep (forward KL) or one base-2 divergence sweep before it (reverse KL, JSD).
-  // 16-bit compute, T = 1, teacher logits from an accumulator (or no teacher), gradients
-  // requested, one GPU.
+  // 16-bit compute, teacher logits from an accumulator (or no teacher), gradients requested, one
+  // GPU; at T != 1 the epilogue also sums the tempered exponentials.
   bool es;
   // Precomputed teacher logits, T = 1, JSD: the row sums come from the base-2 divergence sweep
   // (column parts, caller's teacher logits) instead of the one-warp-per-row JSD sweep.
@@ -124,12 +124,12 @@ struct Plan {
 
 // ORDA_EPILOGUE_STATS=0 turns the epilogue-statistics path off (A/B measurements and tests of the
 // statistics-pass path on the same inputs).
-// The epilogue-statistics path at T != 1 (tempered tile sums, tempered divergence sweeps): on while
-// ORDA_EPILOGUE_STATS_T=1, until it is the default.
+// The epilogue-statistics path at T != 1 (tempered tile sums, tempered divergence sweeps);
+// ORDA_EPILOGUE_STATS_T=0 keeps T != 1 on the statistics-pass path (A/B measurements).
 bool epilogue_stats_tempered() {
   static const bool on = [] {
     const char* e = getenv("ORDA_EPILOGUE_STATS_T");
-    return e && e[0] == '1';
+    return !(e && e[0] == '0');
   }();
   return on;
 }
