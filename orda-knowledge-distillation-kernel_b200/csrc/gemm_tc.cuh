@@ -48,6 +48,10 @@ struct StoreEpiParams {
 struct TcGemmParams {
   CUtensorMap a0, b0, a1, b1;
   CUtensorMap ws_s_map, ws_t_map;  // wide kernel: TMA stores of the shifted logits [rows, ld_ws], 64 x 32 boxes
+  // wide kernel, store epilogue with st_tma = 1: the 16-bit output [M, N] (64 x 32 boxes, 128-byte
+  // swizzle); the epilogue stages each 32-row x 64-column piece in shared memory and stores it by TMA
+  CUtensorMap out_map;
+  int32_t st_tma;
   int32_t m_tiles, n_tiles;
   int32_t kb0, kb1;  // k blocks of segment 0 / 1
   int32_t group_m;

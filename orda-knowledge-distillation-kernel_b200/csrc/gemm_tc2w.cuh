@@ -42,7 +42,7 @@ struct WideShape {
   // part of the drain the next tile's MMAs wait for is halved.
   static constexpr int kEpiWarps = 8;
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
-  static constexpr uint32_t kStaging = EPI == EPI_FWD_STATS ? kEpiWarps * kWideStagingPerWarp : 0;
+  static constexpr uint32_t kStaging = kEpiWarps * kWideStagingPerWarp;  // both epilogues stage via TMA
   static constexpr uint32_t kBarBytes = (2 * kStages + 4) * 8 + 16;
   static constexpr uint32_t kSmemBytes = kStages * kWideStageBytes + kStaging + kBarBytes + 1024;
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
@@ -179,6 +179,59 @@ __device__ __forceinline__ void wide_tile_sums(const FwdEpiParams& p, int64_t ro
       rec[1] = (accT[0] + accT[1]) + (accT[2] + accT[3]);
     } else {
       p.tile_sums[(row * p.n_vtiles + tile0 + h) * 2 + (student ? 0 : 1)] = s1;
+    }
+  }
+}
+
+// Store epilogue through shared memory and TMA (16-bit output, N a multiple of 64, rows not routed to
+// peers): the warp's 32 rows x 256 columns leave as four 32 x 64 TMA stores of full 128-byte lines,
+// instead of 16-byte stores one row per lane. When accumulating, each lane's previous 64 values are
+// loaded before the TMEM wait and added in fp32 before the one rounding.
+template <typename T16>
+__device__ __forceinline__ void wide_store_tma(const TcGemmParams& p, uint32_t tbase, uint32_t staging, int64_t y0,
+                                               int64_t n0, int lane) {
+  const StoreEpiParams& st = p.st;
+  const int64_t row = y0 + lane;
+  const bool row_ok = row < st.M;
+#pragma unroll 1
+  for (int g = 0; g < kPairBN / 64; ++g) {
+    const int64_t c0 = n0 + g * 64;
+    uint4 prev[8];
+    const bool acc = st.accumulate && row_ok && c0 < st.N;
+    if (acc) {
+      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T16*>(st.out) + row * st.ldo + c0);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) prev[q] = src[q];
+    }
+    uint32_t r[2][32];
+    tmem_ld32_async(tbase + g * 64, r[0]);
+    tmem_ld32_async(tbase + g * 64 + 32, r[1]);
+    tmem_wait_ld();
+    if (c0 >= st.N) continue;  // warp-uniform
+    // the previous TMA store of this warp must have read the staging buffer
+    if (lane == 0) bulk_wait_read_all();
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(r[q >> 2][(q & 3) * 8 + e]);
+      if (acc) {
+        const T16* ph = reinterpret_cast<const T16*>(&prev[q]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] += Conv<T16>::to_f(ph[e]);
+      }
+      const uint32_t addr = staging + static_cast<uint32_t>(lane) * 128u +
+                            ((static_cast<uint32_t>(q) ^ static_cast<uint32_t>(lane & 7)) << 4);
+      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pack2<T16>(v[0], v[1])),
+                   "r"(pack2<T16>(v[2], v[3])), "r"(pack2<T16>(v[4], v[5])), "r"(pack2<T16>(v[6], v[7]))
+                   : "memory");
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(&p.out_map, staging, static_cast<int32_t>(c0), static_cast<int32_t>(y0));
+      bulk_commit_group();
     }
   }
 }
@@ -451,10 +504,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WideShape<EPI>::kThr
                               y0, n0, !tdist, lane, j ? lab[1] : lab[0]);
           }
         } else {
-          const int64_t row = static_cast<int64_t>(mt) * 512 + j * 256 + rank * 128 + quarter * 32 + lane;
-          StoreEpiParams st = p.st;
-          if (ks_n > 1) st.out = static_cast<uint8_t*>(st.out) + ks * p.split_bytes;
-          store_epilogue<T16>(st, tbase, row, n0, kPairBN);
+          const int64_t y0 = static_cast<int64_t>(mt) * 512 + j * 256 + rank * 128 + quarter * 32;
+          if (p.st_tma) {
+            wide_store_tma<T16>(p, tbase, staging, y0, n0, lane);
+          } else {
+            StoreEpiParams st = p.st;
+            if (ks_n > 1) st.out = static_cast<uint8_t*>(st.out) + ks * p.split_bytes;
+            store_epilogue<T16>(st, tbase, y0 + lane, n0, kPairBN);
+          }
         }
         tc_fence_before();
         __syncwarp();
@@ -486,9 +543,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WideShape<EPI>::kThr
       }
       if (prof) busy += clk() - c1;
     }
-    if constexpr (EPI == EPI_FWD_STATS) {
+    if (EPI == EPI_FWD_STATS || p.st_tma) {
       if (lane == 0) bulk_wait_all();  // staged stores complete before the shared memory goes away
-    } else {
+    }
+    if constexpr (EPI != EPI_FWD_STATS) {
       // stores routed to other GPUs are visible system-wide once this kernel has finished
       if (p.st.peers > 0) __threadfence_system();
     }
