@@ -52,6 +52,9 @@ struct TcGemmParams {
   // swizzle); the epilogue stages each 32-row x 64-column piece in shared memory and stores it by TMA
   CUtensorMap out_map;
   int32_t st_tma;
+  // with st_tma and rows routed to peers (st.peers > 0, slab_rows a multiple of 512): map k covers
+  // this GPU's slot [slab_rows, N] in peer k's slot buffer
+  CUtensorMap peer_maps[ORDA_MAX_PEERS];
   int32_t m_tiles, n_tiles;
   int32_t kb0, kb1;  // k blocks of segment 0 / 1
   int32_t group_m;

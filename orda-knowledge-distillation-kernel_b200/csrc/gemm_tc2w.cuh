@@ -183,9 +183,9 @@ __device__ __forceinline__ void wide_tile_sums(const FwdEpiParams& p, int64_t ro
   }
 }
 
-// Store epilogue through shared memory and TMA (16-bit output, N a multiple of 64, rows not routed to
-// peers): the warp's 32 rows x 256 columns leave as four 32 x 64 TMA stores of full 128-byte lines,
-// instead of 16-byte stores one row per lane. When accumulating, each lane's previous 64 values are
+// Store epilogue through shared memory and TMA (16-bit output, N a multiple of 64; rows routed to
+// peers go to the owner's slot through that owner's map): the warp's 32 rows x 256 columns leave as
+// four 32 x 64 TMA stores of full 128-byte lines, instead of 16-byte stores one row per lane. When accumulating, each lane's previous 64 values are
 // loaded before the TMEM wait and added in fp32 before the one rounding.
 template <typename T16>
 __device__ __forceinline__ void wide_store_tma(const TcGemmParams& p, uint32_t tbase, uint32_t staging, int64_t y0,
@@ -197,9 +197,10 @@ __device__ __forceinline__ void wide_store_tma(const TcGemmParams& p, uint32_t t
   for (int g = 0; g < kPairBN / 64; ++g) {
     const int64_t c0 = n0 + g * 64;
     uint4 prev[8];
-    const bool acc = st.accumulate && row_ok && c0 < st.N;
+    const T16* prev_base = static_cast<const T16*>(st.peers > 0 ? st.acc_src : st.out);
+    const bool acc = st.accumulate && prev_base && row_ok && c0 < st.N;
     if (acc) {
-      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T16*>(st.out) + row * st.ldo + c0);
+      const uint4* src = reinterpret_cast<const uint4*>(prev_base + row * st.ldo + c0);
 #pragma unroll
       for (int q = 0; q < 8; ++q) prev[q] = src[q];
     }
@@ -230,7 +231,13 @@ __device__ __forceinline__ void wide_store_tma(const TcGemmParams& p, uint32_t t
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
-      tma_store_2d(&p.out_map, staging, static_cast<int32_t>(c0), static_cast<int32_t>(y0));
+      if (st.peers > 0) {  // the whole 512-row tile belongs to one owner (slab_rows % 512 == 0)
+        const int64_t owner = y0 / st.slab_rows;
+        tma_store_2d(&p.peer_maps[owner], staging, static_cast<int32_t>(c0),
+                     static_cast<int32_t>(y0 - owner * st.slab_rows));
+      } else {
+        tma_store_2d(&p.out_map, staging, static_cast<int32_t>(c0), static_cast<int32_t>(y0));
+      }
       bulk_commit_group();
     }
   }

@@ -492,9 +492,18 @@ int dw_tc(const orda_distill_args_t* a, const Plan& P, const void* dz0, const vo
   if ((rc = make_operand_map(&prm.b0, dt, h0, true, n, rows, ldh0, 128))) return rc;
   prm.kb0 = static_cast<int32_t>(cdiv(rows, kBK));
   prm.st = StoreEpiParams{out, n, a->vocab, n, out_f32, accumulate};
-  // 16-bit dW not routed to peers: stage the tiles in shared memory and store them by TMA
-  if (!route && !out_f32 && n % 64 == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0) {
+  // 16-bit dW: stage the tiles in shared memory and store them by TMA, into `out` or, routed, into
+  // the owners' slots (one map per owner; needs owner slabs of whole 512-row tiles)
+  if (!out_f32 && n % 64 == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0 &&
+      (!route || route->slab_rows % 512 == 0)) {
     if ((rc = make_map(&prm.out_map, dt, out, n, a->vocab, n, 64, 32))) return rc;
+    if (route) {
+      for (int k = 0; k < route->world; ++k) {
+        const uint8_t* slot = static_cast<const uint8_t*>(route->slot_base[k]) +
+                              static_cast<int64_t>(route->rank) * route->slab_rows * n * 2;
+        if ((rc = make_map(&prm.peer_maps[k], dt, slot, n, route->slab_rows, n, 64, 32))) return rc;
+      }
+    }
     prm.st_tma = 1;
   }
   if (route) {
