@@ -213,7 +213,8 @@ int32_t orda_distill_fwdbwd_static_ws(const orda_distill_args_t* args, void* str
 typedef struct orda_peer_slots {
   int32_t world;                        /* ranks (1..ORDA_MAX_PEERS)                                 */
   int32_t rank;                         /* this rank                                                 */
-  int64_t slab_rows;                    /* lm_head rows owned per rank (ceil(vocab / world) or more)  */
+  int64_t slab_rows;                    /* lm_head rows owned per rank (>= ceil(vocab / world); a
+                                           multiple of 512 lets the dW epilogue store by TMA)        */
   void* slot_base[ORDA_MAX_PEERS];      /* device address of rank k's slots buffer, as mapped here   */
   void* grad_base[ORDA_MAX_PEERS];      /* device address of rank k's grad buffer, as mapped here    */
 } orda_peer_slots_t;

@@ -98,7 +98,8 @@ class PeerGradientExchange:
             raise ValueError("peer gradient exchange needs hidden % 8 == 0")
         dev = weight.device
         self.vocab, self.hidden, self.dtype = vocab, hidden, weight.dtype
-        self.slab = -(-vocab // self.world)
+        # whole 512-row dW tiles per owner, so the dW epilogue can store routed rows by TMA
+        self.slab = -(-(-(-vocab // self.world)) // 512) * 512
         self.slots = torch.empty((self.world * self.slab, hidden), dtype=weight.dtype, device=dev)
         self.grad = torch.empty((vocab, hidden), dtype=weight.dtype, device=dev)
         # every rank maps the other ranks' two buffers (CUDA IPC; plain peer mappings over NVLink)
