@@ -67,6 +67,8 @@ def _args():
     p.add_argument("--dw-exchange", default="nccl", choices=["peer", "nccl"],
                    help="N>1: sum the lm_head gradient through peer memory (fused into the dW GEMM's epilogue) "
                         "or with an NCCL all-reduce")
+    p.add_argument("--peer-reduce-ctas", type=int, default=64,
+                   help="N>1 with --dw-exchange peer: CTAs of the owners' reduce-and-broadcast kernel")
     p.add_argument("--reserve-sms", type=int, default=-1,
                    help="SMs the dHidden GEMM leaves to the overlapped dW all-reduce (N>1; -1: default)")
     return p.parse_args()
@@ -736,7 +738,7 @@ def run_ours(args):
     if pg is not None and args.dw_exchange == "peer":
         from orda_ce_kernel.parallel import PeerGradientExchange
 
-        exchange = PeerGradientExchange(w, group=pg)
+        exchange = PeerGradientExchange(w, group=pg, reduce_ctas=args.peer_reduce_ctas)
     reserve = (args.reserve_sms if args.reserve_sms >= 0 else default_reserve_sms(world)) \
         if pg is not None and exchange is None else 0
 
