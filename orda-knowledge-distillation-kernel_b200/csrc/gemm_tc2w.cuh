@@ -104,33 +104,30 @@ __device__ __forceinline__ void wide_fwd_acc(const FwdEpiParams& p, const CUtens
     }
     if (write_ws) {
       const float mL = m * kLog2e;
-      // four 32-column pieces through two 2 KB staging buffers (64-byte swizzle): piece p is packed
-      // while the TMA store of piece p - 1 still reads the other buffer
 #pragma unroll
-      for (int pc = 0; pc < 4; ++pc) {
-        const uint32_t buf = staging + static_cast<uint32_t>(pc & 1) * 2048u;
-        // the store that last used this buffer (two pieces ago) must have read it
-        if (lane == 0) bulk_wait_read_one();
+      for (int hf = 0; hf < 2; ++hf) {
+        // the previous TMA store of this warp must have read the staging buffer
+        if (lane == 0) bulk_wait_read_all();
         __syncwarp();
-        // row `lane`, 32 columns: 16-byte chunk q of the 64-byte row lands at q ^ ((lane >> 1) & 3)
+        // row `lane`, 64 columns: 16-byte chunk q of the 128-byte row lands at q ^ (lane & 7)
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int e0 = q * 8;
+        for (int q = 0; q < 8; ++q) {
+          const int c = hf * 2 + (q >> 2), e0 = (q & 3) * 8;
           // base-2 exponents relative to the tile maximum: (z - m) * log2 e
-          auto y = [&](int e) { return fmaf(__uint_as_float(r[pc][e]), kLog2e, -mL); };
+          auto y = [&](int e) { return fmaf(__uint_as_float(r[c][e]), kLog2e, -mL); };
           const uint32_t w0 = pack2<WsT>(y(e0), y(e0 + 1));
           const uint32_t w1 = pack2<WsT>(y(e0 + 2), y(e0 + 3));
           const uint32_t w2 = pack2<WsT>(y(e0 + 4), y(e0 + 5));
           const uint32_t w3 = pack2<WsT>(y(e0 + 6), y(e0 + 7));
-          const uint32_t addr = buf + static_cast<uint32_t>(lane) * 64u +
-                                ((static_cast<uint32_t>(q) ^ ((static_cast<uint32_t>(lane) >> 1) & 3u)) << 4);
+          const uint32_t addr = staging + static_cast<uint32_t>(lane) * 128u +
+                                ((static_cast<uint32_t>(q) ^ static_cast<uint32_t>(lane & 7)) << 4);
           asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w0), "r"(w1), "r"(w2), "r"(w3)
                        : "memory");
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(ws_map, buf, static_cast<int32_t>(nh + pc * 32), static_cast<int32_t>(y0));
+          tma_store_2d(ws_map, staging, static_cast<int32_t>(nh + hf * 64), static_cast<int32_t>(y0));
           bulk_commit_group();
         }
       }

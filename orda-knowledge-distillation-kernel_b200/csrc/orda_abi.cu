@@ -51,7 +51,7 @@ EncodeTiledFn encode_fn() {
 
 // 2-D tensor map over a row-major [outer, inner] array of 16-bit elements with a 128B-swizzled box.
 int make_map(CUtensorMap* m, int dtype, const void* base, uint64_t inner, uint64_t outer, uint64_t ld_elems,
-             uint32_t box_inner, uint32_t box_outer, bool swizzle64 = false) {
+             uint32_t box_inner, uint32_t box_outer) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return ORDA_ERR_CUDA;
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (ld_elems * 2) % 16 != 0) return ORDA_ERR_ALIGNMENT;
@@ -61,8 +61,7 @@ int make_map(CUtensorMap* m, int dtype, const void* base, uint64_t inner, uint64
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = fn(m, dtype == ORDA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                         const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        swizzle64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? ORDA_OK : ORDA_ERR_INVALID_ARGUMENT;
 }
@@ -399,10 +398,10 @@ FwdEpiParams fwd_params(const orda_distill_args_t* a, const Plan& P, uint8_t* ws
 int ws_store_maps(const orda_distill_args_t* a, const Plan& P, uint8_t* ws, const ChunkPtrs& c, TcGemmParams& prm) {
   int rc;
   if (P.write_ws_s &&
-      (rc = make_map(&prm.ws_s_map, a->compute_dtype, ws + P.off_ws_s, P.vpad, c.rows, P.vpad, 32, 32, true)))
+      (rc = make_map(&prm.ws_s_map, a->compute_dtype, ws + P.off_ws_s, P.vpad, c.rows, P.vpad, 64, 32)))
     return rc;
   if (P.teacher_acc && P.write_ws_t &&
-      (rc = make_map(&prm.ws_t_map, a->compute_dtype, ws + P.off_ws_t, P.vpad, c.rows, P.vpad, 32, 32, true)))
+      (rc = make_map(&prm.ws_t_map, a->compute_dtype, ws + P.off_ws_t, P.vpad, c.rows, P.vpad, 64, 32)))
     return rc;
   return ORDA_OK;
 }

@@ -186,11 +186,6 @@ __device__ __forceinline__ void bulk_wait_read_all() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 // Wait until every committed bulk store of this thread has completed.
-// At most one committed bulk group of this thread may still be reading its shared-memory source.
-__device__ __forceinline__ void bulk_wait_read_one() {
-  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-}
-
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // Orders this thread's completed async-proxy (TMA) writes to global memory before its later
